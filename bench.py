@@ -1,0 +1,449 @@
+#!/usr/bin/env python3
+"""Benchmark of the W4A16 GEMM hot path on B200 -- one JSON line on rank 0.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the config the headline metric is quoted on):
+the decode sweep M in {1, 4, 8, 16} x Llama-3-8B projections (N x K) 4096x4096,
+1024x4096, 14336x4096, 4096x14336, G = 128.  One *step* runs all 16 GEMMs once,
+each on its own weight copy (286 MB of packed weights per step, > 2x the 126 MB
+L2, so nothing is served from L2 between uses).  Inputs are seeded synthetic
+data with BASELINE's distributions (x ~ N(0,1) fp16, q ~ U{0..15}, scales ~
+U[0.002, 0.02] fp16), resident in HBM before the timed region.
+
+* value       -- algorithmic bytes (packed weights + scales + x + y) of all GEMMs
+                 per second, device-timed (CUDA events around K CUDA-graph replays).
+* e2e         -- the same metric through the public API (w4a16_opt.w4a16_gemm),
+                 eager calls, with each step's activations copied host->device from
+                 pinned memory and its outputs read back device->host.
+* roofline    -- achieved bytes/s of the decode kernel vs the measured HBM copy
+                 bandwidth (MEASURED_PEAKS.json), plus the ncu DRAM traffic per launch
+                 from profiles/ when a capture of this workload is committed.
+* prefill     -- BASELINE configs[2] (M in {128, 512, 2048, 8192} x 14336x4096 /
+                 4096x14336 x G in {64, 128}) in TFLOP/s against the measured dense
+                 fp16/bf16 tensor peak (N = 1 only).
+* cpu_baseline -- the reference's CPU path (fp16 dequant + fp32 matmul, torch CPU,
+                 all host threads) over one pass of the same 16 GEMMs.
+
+With N > 1 (torchrun, one rank per GPU, NCCL) every projection is tensor-parallel
+over the N ranks: q/o and down split K (fp32 all-reduce), k/v and gate/up split N
+(all-gather).  Total work is fixed, so scaling is "strong"; time is the max over
+ranks.  ``--impl reference`` times the CPU reference path alone (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import csv
+import io
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "w4a16-gemm_b200")
+for _p in (ROOT, PKG):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+METRIC = "HBM GB/s at M≤16 & TFLOP/s at M≥128, 1–8 B200, % of roofline"
+DECODE_SHAPES = (("q/o", 4096, 4096), ("k/v", 1024, 4096), ("gate/up", 14336, 4096), ("down", 4096, 14336))
+DECODE_M = (1, 4, 8, 16)
+DECODE_G = 128
+TP_SPLIT = {"q/o": "row", "k/v": "col", "gate/up": "col", "down": "row"}
+PREFILL_M = (128, 512, 2048, 8192)
+PREFILL_SHAPES = ((14336, 4096), (4096, 14336))
+PREFILL_G = (64, 128)
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def alg_bytes(M, N, K, G):
+    """Bytes a W4A16 GEMM must move at least once: packed weights, scales, x, y."""
+    return N * K // 2 + 2 * N * (K // G) + 2 * M * K + 2 * M * N
+
+
+def make_inputs(M, N, K, G, seed, device):
+    """Seeded BASELINE inputs: x fp16 [M,K], q uint8 [N,K] (CPU), scales fp16, packed Wp."""
+    from w4a16_opt import pack_int4
+    gen = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, K, generator=gen).half()
+    q = torch.randint(0, 16, (N, K), generator=gen, dtype=torch.uint8)
+    scales = (torch.rand(K // G, N, generator=gen) * 0.018 + 0.002).half()
+    if device == "cpu":
+        return x, q, scales, None
+    Wp = pack_int4(q.to(device))
+    return x.to(device), q, scales.to(device), Wp
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            d = json.load(f)
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def __enter__(self):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            time.sleep(0.25)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+        self.file.flush()
+
+    def summary(self):
+        rows = []
+        try:
+            with open(self.file.name) as f:
+                for r in csv.reader(f):
+                    if len(r) >= 9:
+                        rows.append([c.strip() for c in r])
+        finally:
+            os.unlink(self.file.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no nvidia-smi samples"], "samples": 0}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        smax = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(smax) if smax else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def smi_index(local):
+    """nvidia-smi index of this process's CUDA device (honours CUDA_VISIBLE_DEVICES)."""
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        if local < len(ids):
+            return ids[local]
+    return str(local)
+
+
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def max_over_ranks(v, world):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def graph_time_ms(step_fn, steps, warmup, world):
+    """Capture one step in a CUDA graph, replay W untimed then K timed; device ms (max over ranks)."""
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        step_fn()
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step_fn()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        g.replay()
+    t1.record()
+    t1.synchronize()
+    torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(t0.elapsed_time(t1), world)
+    del g
+    return ms
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of a kernel from a committed ncu summary (profiles/<name>.json)."""
+    path = os.path.join(ROOT, "profiles", name + ".json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f)
+
+
+def cpu_reference_pass(units, threads):
+    """One pass of the reference's CPU path over the given (x, q, scales, G) units; seconds."""
+    from oracle import cpu_reference
+    torch.set_num_threads(threads)
+    t0 = time.perf_counter()
+    for x, q, s, G in units:
+        cpu_reference.ref_gemm(x, q, s, G)
+    return time.perf_counter() - t0
+
+
+# ---------------------------------------------------------------------------------------------- ours
+
+def run_ours(args):
+    world, rank, local = dist_env()
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    import w4a16_opt
+    from w4a16_opt import tp
+
+    # ---- decode sweep units (inputs identical on every rank: same seeds)
+    units, step_bytes, in_bytes, out_bytes = [], 0, 0, 0
+    seed = 1000
+    for name, N, K in DECODE_SHAPES:
+        for M in DECODE_M:
+            x, q, s, Wp = make_inputs(M, N, K, DECODE_G, seed, "cuda")
+            seed += 1
+            u = {"name": name, "M": M, "N": N, "K": K, "x": x, "q": q, "s": s, "Wp": Wp}
+            if world == 1:
+                u["y"] = torch.empty(M, N, dtype=torch.float16, device="cuda")
+            elif TP_SPLIT[name] == "col":
+                layer = tp.ColumnParallelW4A16(Wp, s, N, K)
+                u.update(layer=layer, y_local=torch.empty(M, N // world, dtype=torch.float16, device="cuda"),
+                         y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
+                del u["Wp"]
+            else:
+                layer = tp.RowParallelW4A16(Wp, s, N, K)
+                u.update(layer=layer, x_local=layer.x_slice(x),
+                         part=torch.empty(M, N, dtype=torch.float32, device="cuda"))
+                del u["Wp"]
+            units.append(u)
+            step_bytes += alg_bytes(M, N, K, DECODE_G)
+            in_bytes += 2 * M * K
+            out_bytes += 2 * M * N
+    torch.cuda.synchronize()
+
+    def step():
+        for u in units:
+            if world == 1:
+                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"])
+            elif "x_local" in u:
+                u["layer"].partial(u["x_local"], out=u["part"])
+                u["layer"].reduce(u["part"])
+            else:
+                u["layer"].local(u["x"], out=u["y_local"])
+                u["layer"].gather(u["y_local"], out=u["y"])
+
+    with ClockSampler(smi_index(local)) as clocks:
+        ms = graph_time_ms(step, args.steps, args.warmup, world)
+    ms_step = ms / args.steps
+    value = step_bytes * args.steps / (ms / 1e3) / 1e9
+
+    # ---- e2e through the public API: pinned host activations in, results out, every step
+    e2e = None
+    if world == 1:
+        host_x = [u["x"].cpu().pin_memory() for u in units]
+        host_y = [torch.empty(u["M"], u["N"], dtype=torch.float16).pin_memory() for u in units]
+        dev_x = [torch.empty_like(u["x"]) for u in units]
+
+        def e2e_step():
+            for u, hx, hy, dx in zip(units, host_x, host_y, dev_x):
+                dx.copy_(hx, non_blocking=True)
+                y = w4a16_opt.w4a16_gemm(u["Wp"], dx, u["s"])
+                hy.copy_(y, non_blocking=True)
+            torch.cuda.current_stream().synchronize()
+
+        e2e_steps = max(3, min(args.steps, 500))
+        for _ in range(max(3, args.warmup // 10)):
+            e2e_step()
+        t0 = time.perf_counter()
+        for _ in range(e2e_steps):
+            e2e_step()
+        e2e_s = time.perf_counter() - t0
+        e2e = {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": "GB/s",
+               "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
+               "api": "w4a16_opt.w4a16_gemm (eager, current stream)"}
+
+    peaks, peak_kind = load_peaks()
+    traffic = profile_traffic("decode_traffic")
+    roofline = {"bound": "hbm", "kernel": "w4a16::decode_kernel", "achieved": round(value, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(value / peaks["hbm_gbs"], 4),
+                "peak_source": f"hbm_gbs ({peak_kind})",
+                "traffic": None if traffic is None else traffic.get("bytes_per_step_scaled"),
+                "algorithmic_bytes_per_step": step_bytes}
+    if world > 1:
+        roofline["note"] = "per-rank time includes the NCCL collectives of the TP split"
+
+    # ---- prefill, N = 1
+    prefill = None
+    if world == 1 and not args.no_prefill:
+        punits, pflops, pbytes = [], 0, 0
+        for (N, K) in PREFILL_SHAPES:
+            for G in PREFILL_G:
+                for M in PREFILL_M:
+                    x, q, s, Wp = make_inputs(M, N, K, G, seed, "cuda")
+                    seed += 1
+                    punits.append((Wp, x, s, torch.empty(M, N, dtype=torch.float16, device="cuda")))
+                    pflops += 2 * M * N * K
+                    pbytes += alg_bytes(M, N, K, G)
+        torch.cuda.synchronize()
+
+        def pstep():
+            for Wp, x, s, y in punits:
+                w4a16_opt.w4a16_gemm_out(Wp, x, s, y)
+
+        psteps = max(3, args.prefill_steps)
+        pms = graph_time_ms(pstep, psteps, 3, world)
+        tflops = pflops * psteps / (pms / 1e3) / 1e12
+        prefill = {"workload": "configs[2]: M in {128,512,2048,8192} x (14336x4096, 4096x14336) x G in {64,128}",
+                   "value": round(tflops, 1), "unit": "TFLOP/s", "steps": psteps, "ms_per_step": round(pms / psteps, 4),
+                   "gpu_launches": len(punits) * psteps,
+                   "roofline": {"bound": "tensor", "kernel": "w4a16::prefill_kernel", "achieved": round(tflops, 1),
+                                "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                                "frac": round(tflops / peaks["bf16_tflops"], 4),
+                                "peak_source": f"bf16_tflops burst ({peak_kind}; dense fp16 = bf16 rate)",
+                                "frac_of_sustained": round(tflops / peaks["bf16_tflops_sustained"], 4)}}
+        del punits
+
+    # ---- CPU baseline: the reference's CPU path, one pass over the 16 decode GEMMs (rank 0, N = 1)
+    cpu = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cunits = [(u["x"].cpu(), u["q"], u["s"].cpu(), DECODE_G) for u in units]
+        threads = os.cpu_count() or 1
+        secs = cpu_reference_pass(cunits, threads)
+        cpu = {"value": round(step_bytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+               "seconds": round(secs, 2),
+               "sample": "one pass over the 16 GEMMs of the decode sweep (fp16 dequant + fp32 matmul, torch CPU)"}
+
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    out = {
+        "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "data": "synthetic (seeded: x~N(0,1) fp16, q~U{0..15}, scales~U[0.002,0.02] fp16)",
+        "config": {"workload": "configs[1] decode sweep: M in {1,4,8,16} x Llama-3-8B (N x K) "
+                               "4096x4096, 1024x4096, 14336x4096, 4096x14336, G=128",
+                   "gemms_per_step": len(units), "algorithmic_bytes_per_step": step_bytes,
+                   "l2": "inputs larger than L2: 16 distinct weight copies, %d MB per step vs 126 MB L2"
+                         % (step_bytes // 2**20),
+                   "parallelism": "single GPU" if world == 1 else f"tp{world} (col: k/v, gate/up; row: q/o, down)",
+                   "timing": "CUDA graph of one step, K replays between CUDA events, max over ranks"},
+        "e2e": e2e, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
+        "clocks": clocks.summary(), "gpu_launches": len(units) * args.steps,
+    }
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------------------------------------- reference
+
+def run_reference(args):
+    """The reference's CPU implementation of the path (its tests/quant.py dequant + torch
+    matmul, restated in oracle/cpu_reference.py) on this host's cores; rank 0 only."""
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    from oracle import cpu_reference
+    units, seed = [], 1000
+    for name, N, K in DECODE_SHAPES:
+        for M in DECODE_M:
+            x, q, s, _ = make_inputs(M, N, K, DECODE_G, seed, "cpu")
+            seed += 1
+            units.append((x, q, s, M, N, K))
+    # each step is one GEMM of the sweep, cycling through the 16 (a bounded sample per step)
+    for i in range(args.warmup):
+        x, q, s, *_ = units[i % len(units)]
+        cpu_reference.ref_gemm(x, q, s, DECODE_G)
+    total, t0 = 0, time.perf_counter()
+    for i in range(args.steps):
+        x, q, s, M, N, K = units[i % len(units)]
+        cpu_reference.ref_gemm(x, q, s, DECODE_G)
+        total += alg_bytes(M, N, K, DECODE_G)
+    secs = time.perf_counter() - t0
+    value = total / secs / 1e9
+    sample = "step i = GEMM i mod 16 of the decode sweep (fp16 dequant + fp32 matmul, torch CPU)"
+    out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+           "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
+           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+           "data": "synthetic (seeded, same inputs as the GPU arm)",
+           "config": {"workload": "configs[1] decode sweep (CPU reference path)", "threads": threads},
+           "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+                            "sample": sample},
+           "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--prefill-steps", type=int, default=40)
+    ap.add_argument("--no-prefill", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        args.steps = 16 if args.steps is None else args.steps
+        args.warmup = 3 if args.warmup is None else args.warmup
+        return run_reference(args)
+    args.steps = 20000 if args.steps is None else args.steps
+    args.warmup = 200 if args.warmup is None else args.warmup
+    if args.warmup < 3:
+        args.warmup = 3
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if args.gpus != world:
+        print(f"bench.py: --gpus {args.gpus} but WORLD_SIZE={world}; launch N>1 with torchrun", file=sys.stderr)
+        if world == 1 and args.gpus > 1:
+            return 2
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,115 @@
+/*
+ * w4a16.h -- C ABI of the B200 (sm_100a) W4A16 GEMM.
+ *
+ *     y[M, N] = x[M, K] @ W^T,   W[n, k] = (q[n, k] - 8) * scales[k / G, n]
+ *
+ * x: fp16 [M, K] row-major.  q: 4-bit codes packed into int32 words in the
+ * mma.m16n8k16 fragment order of the reference format (word index
+ * (((n/16)*(K/64) + k/64)*32 + lane)*4 + (k%64)/16; nibble i of a lane's word
+ * holds n = g + 8*((i&3)&1), k = 2t + 8*((i&3)>>1) + (i>>2), g = lane/4,
+ * t = lane%4).  scales: fp16 [groups, N] with G = K / groups in {64, 128}.
+ *
+ * All pointers are CUDA device pointers; `stream` is a cudaStream_t (NULL =
+ * legacy default stream).  Functions return W4A16_OK or an error status; the
+ * human-readable reason of the last failure on the calling thread is available
+ * from w4a16_last_error().  No function allocates device memory, so GEMM
+ * launches may be captured in CUDA graphs.
+ *
+ * This header replaces the reference's torch-typed entry point
+ *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)
+ * (akshay919191/W4A16-GEMM src/vectorized/kernel.cu:218, bound as
+ * w4a16_opt.w4a16_gemm in src/vectorized/extension.cpp:5-8) with plain
+ * pointers and sizes.
+ */
+#ifndef W4A16_H_
+#define W4A16_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W4A16_ABI_VERSION 1
+
+typedef enum w4a16_status {
+    W4A16_OK = 0,
+    W4A16_ERR_NULL_POINTER = 1,      /* a required pointer is NULL */
+    W4A16_ERR_VARIANT = 2,           /* "variant must be -1 (auto), 0 (decode) or 1..4" (kernel.cu:224) */
+    W4A16_ERR_M = 3,                 /* "M must be at least 1" (kernel.cu:227) */
+    W4A16_ERR_DIM_RANGE = 4,         /* "dimensions must fit in int32" (kernel.cu:228) */
+    W4A16_ERR_K_MULTIPLE = 5,        /* "K must be a multiple of 64" (kernel.cu:230) */
+    W4A16_ERR_N_MULTIPLE = 6,        /* "N must be a multiple of 16" (kernel.cu:231) */
+    W4A16_ERR_GROUPS = 7,            /* "K must be divisible by the number of groups" (kernel.cu:232) */
+    W4A16_ERR_WP_SIZE = 8,           /* "Wp must hold N*K/8 words" (kernel.cu:233) */
+    W4A16_ERR_ALIGNMENT = 9,         /* "Wp, x and scales must be 16-byte aligned" (kernel.cu:234-237) */
+    W4A16_ERR_GROUP_SIZE = 10,       /* "unsupported group size G, supported: 64, 128" (kernel.cu:240) */
+    W4A16_ERR_DECODE_SHAPE = 11,     /* "decode kernel needs M in [1, 16], ..." (kernel.cu:246-249) */
+    W4A16_ERR_OUT_DTYPE = 12,        /* out_dtype is not a w4a16_out_dtype value */
+    W4A16_ERR_DEVICE = 13,           /* current device is not an sm_100 GPU */
+    W4A16_ERR_CUDA = 14,             /* a CUDA runtime / driver call failed */
+    W4A16_ERR_DEVICE_TIMEOUT = 15    /* a kernel's bounded wait ran out (see w4a16_device_status) */
+} w4a16_status;
+
+typedef enum w4a16_out_dtype {
+    W4A16_OUT_F16 = 0,               /* y is fp16 [M, N] (the reference's output) */
+    W4A16_OUT_F32 = 1                /* y is fp32 [M, N] (row-parallel partial sums) */
+} w4a16_out_dtype;
+
+typedef struct w4a16_route {
+    int32_t kernel;     /* 0 = decode (M <= 16 weight-streaming GEMV), 1 = prefill (tcgen05) */
+    int32_t config;     /* prefill tile config 1..4 (token tile 32/64/128/256); 0 for decode */
+    int32_t tile_m;     /* tokens per tile (decode: 8 or 16 padded rows) */
+    int32_t tile_n;     /* output channels per tile (decode 64, prefill 128) */
+    int32_t split_k;    /* K splits (decode cluster size; 1 for prefill) */
+    int32_t grid;       /* CTAs launched */
+    int32_t stages;     /* pipeline depth */
+    int32_t smem_bytes; /* dynamic shared memory per CTA */
+} w4a16_route;
+
+/* Version of this ABI (W4A16_ABI_VERSION). */
+int32_t w4a16_abi_version(void);
+
+/* Validate a GEMM call without launching anything.  Checks, in the order of
+ * the reference (kernel.cu:224-249): variant range, M >= 1, int32 range,
+ * K % 64, N % 16, K % groups, wp_words == N*K/8, 16-byte alignment of
+ * Wp/x/scales, G = K/groups in {64, 128}, and the decode contract when
+ * variant == 0.  Pointers may be NULL here (alignment is then not checked). */
+w4a16_status w4a16_validate(const void* Wp, const void* x, const void* scales,
+                            int64_t M, int64_t N, int64_t K, int64_t groups,
+                            int64_t wp_words, int32_t variant);
+
+/* y = x @ W^T on `stream`.  variant: -1 auto, 0 decode kernel (reference decode
+ * contract: M <= 16, N % 64 == 0, K % 512 == 0), 1..4 force a prefill tile
+ * config.  out_dtype selects fp16 or fp32 y.  Replaces w4a16_gemm_cuda
+ * (kernel.cu:218-267); unlike it, y is caller-allocated. */
+w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y,
+                        int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
+                        int32_t variant, int32_t out_dtype, void* stream);
+
+/* The launch w4a16_gemm would make for this call (kernel choice, tiles, grid).
+ * Mirrors the reference's routing (kernel.cu:242-249) and prefill config
+ * selection (kernel.cu:140-214).  Queries the current device. */
+w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, int32_t variant,
+                               w4a16_route* out);
+
+/* out[N, K] (fp16) = the dequantised weights, bit-identical to the reference's
+ * dequantize_w4 (tests/quant.py:77-80).  Debug / verification entry. */
+w4a16_status w4a16_dequant(const int32_t* Wp, const void* scales, void* out,
+                           int64_t N, int64_t K, int64_t groups, void* stream);
+
+/* Reads the current device's status word, set by a kernel whose bounded wait
+ * ran out (0 = none).  Synchronises the device.  reset != 0 clears it. */
+w4a16_status w4a16_device_status(int32_t* code, int32_t reset);
+
+/* Short name of a status code. */
+const char* w4a16_status_string(w4a16_status status);
+
+/* Detailed message of the last failing call on this thread ("" if none). */
+const char* w4a16_last_error(void);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif  /* W4A16_H_ */

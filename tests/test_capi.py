@@ -1,0 +1,123 @@
+"""CPU tests of the drop-in boundary: libw4a16.so loads and exports every symbol
+include/w4a16.h declares, host-side validation follows the reference's check
+order and messages (kernel.cu:219-249), and the torch binding's tensor checks."""
+import ctypes
+import os
+import re
+
+import pytest
+import torch
+
+from w4a16_opt import capi
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "w4a16.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(w4a16_[a-z_]+)\s*\(", text)))
+
+
+def test_header_declares_exports_table():
+    assert declared_functions() == sorted(capi.EXPORTS)
+
+
+def test_library_loads_and_exports_every_symbol():
+    lib = capi.load()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+    assert lib.w4a16_abi_version() == 1
+
+
+def test_library_has_no_torch_dependency():
+    # The C ABI is usable from any host language: no libtorch/libc10 in its link map.
+    import subprocess
+    out = subprocess.run(["ldd", capi.library_path()], capture_output=True, text=True).stdout
+    assert "torch" not in out and "c10" not in out
+
+
+def test_status_strings():
+    lib = capi.load()
+    for code, name in capi.STATUS_NAMES.items():
+        assert lib.w4a16_status_string(code).decode() == name
+
+
+def _validate(M=2, N=64, K=512, groups=8, wp_words=None, variant=-1, wp=None, x=None, s=None):
+    lib = capi.load()
+    wp_words = N * K // 8 if wp_words is None else wp_words
+    st = lib.w4a16_validate(wp, x, s, M, N, K, groups, wp_words, variant)
+    return st, capi.last_error(lib)
+
+
+@pytest.mark.parametrize("kw,status,msg", [
+    (dict(variant=7), 2, "variant must be -1 (auto), 0 (decode) or 1..4"),
+    (dict(variant=-2), 2, "variant"),
+    (dict(M=0), 3, "M must be at least 1"),
+    (dict(N=1 << 31, groups=8), 4, "dimensions must fit in int32"),
+    (dict(K=32, groups=1), 5, "multiple of 64"),
+    (dict(N=24), 6, "multiple of 16"),
+    (dict(groups=3), 7, "divisible by the number of groups"),
+    (dict(wp_words=5), 8, "Wp must hold N*K/8 words"),
+    (dict(wp=0x1008), 9, "16-byte aligned"),
+    (dict(groups=16), 10, "unsupported group size 32, supported: 64, 128"),
+    (dict(groups=2), 10, "unsupported group size 256"),
+    (dict(M=32, variant=0), 11, "decode kernel needs"),
+    (dict(N=80, K=640, groups=10, variant=0), 11, "decode kernel needs"),
+])
+def test_validate_rejects(kw, status, msg):
+    st, err = _validate(**kw)
+    assert st == status, (st, err)
+    assert msg in err
+
+
+def test_validate_check_order():
+    # variant is checked before the shapes, K before N, groups before the word count
+    assert _validate(variant=9, M=0)[0] == 2
+    assert _validate(K=32, N=24, groups=1)[0] == 5
+    assert _validate(groups=3, wp_words=1)[0] == 7
+
+
+@pytest.mark.parametrize("kw", [dict(), dict(variant=0), dict(variant=3, M=1000), dict(N=208, K=384, groups=3)])
+def test_validate_accepts(kw):
+    assert _validate(**kw)[0] == 0
+
+
+def test_gemm_null_pointers_rejected():
+    lib = capi.load()
+    st = lib.w4a16_gemm(None, None, None, None, 2, 64, 512, 8, 64 * 512 // 8, -1, 0, None)
+    assert st == 1 and "non-null" in capi.last_error(lib)
+
+
+def test_gemm_bad_out_dtype_rejected():
+    lib = capi.load()
+    p = ctypes.c_void_p(0x10000)
+    st = lib.w4a16_gemm(p, p, p, p, 2, 64, 512, 8, 64 * 512 // 8, -1, 5, None)
+    assert st == 12
+
+
+@pytest.mark.skipif(torch.cuda.is_available(), reason="checks the no-GPU error path")
+def test_query_route_without_gpu_reports_cuda_error():
+    lib = capi.load()
+    r = capi.Route()
+    st = lib.w4a16_query_route(1, 4096, 4096, 32, -1, ctypes.byref(r))
+    assert st in (13, 14)
+
+
+# ---------------------------------------------------------------- torch binding tensor checks (CPU)
+
+def test_binding_rejects_cpu_tensors():
+    from w4a16_opt import w4a16_gemm
+    Wp = torch.zeros(64 * 512 // 8, dtype=torch.int32)
+    x = torch.zeros(2, 512, dtype=torch.half)
+    s = torch.zeros(8, 64, dtype=torch.half)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        w4a16_gemm(Wp, x, s)
+
+
+def test_binding_exports():
+    import w4a16_opt
+    for name in ("w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status"):
+        assert callable(getattr(w4a16_opt, name))
+    assert w4a16_opt.ABI_VERSION == 1

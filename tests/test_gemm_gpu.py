@@ -1,0 +1,364 @@
+"""GPU parity tests for the W4A16 GEMM (B200).  Every case compares the CUDA
+kernels with the CPU oracle on the same seeded inputs.
+
+The matrix mirrors the reference's own suite (tests/test_w4a16.py): decode
+grid, Llama-3-8B shapes, prefill for arbitrary M, ragged N/K, forced prefill
+configs, bitwise equality across configs, row independence, one-hot exactness,
+nibble extremes, hard scale ranges, zero input, determinism, CUDA-graph
+capture and input rejection -- plus the BASELINE configs, the golden vectors,
+the fp32-output mode, direct C-ABI calls and the dequant entry.
+"""
+import ctypes
+import os
+
+import numpy as np
+import pytest
+import torch
+
+from helpers import GS, assert_close, make_problem, make_workload, ref_gemm, to_np
+from oracle import w4a16_oracle as oracle
+
+pytestmark = pytest.mark.gpu
+
+DECODE_SHAPES = [
+    (64, 512), (128, 1024), (256, 2048), (512, 4096),
+    (4096, 4096), (6144, 4096), (4096, 14336), (28672, 4096),
+]
+DECODE_BATCHES = [1, 2, 3, 7, 8, 9, 15, 16]
+PREFILL_VARIANTS = [1, 2, 3, 4]
+PREFILL_M = [17, 31, 32, 33, 63, 64, 65, 100, 127, 128, 129, 300, 512, 1000]
+RAGGED = [(16, 64), (48, 192), (80, 640), (208, 384), (272, 1152)]
+GOLDEN = np.load(os.path.join(os.path.dirname(__file__), "golden", "golden.npz"))
+
+
+@pytest.fixture(autouse=True)
+def _gpu(cuda_device):
+    yield
+
+
+def gemm(*a, **kw):
+    from w4a16_opt import w4a16_gemm
+    return w4a16_gemm(*a, **kw)
+
+
+# ---------------------------------------------------------------- decode
+
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", DECODE_BATCHES)
+@pytest.mark.parametrize("N,K", DECODE_SHAPES[:4])
+def test_shapes(M, N, K, G):
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales), ref_gemm(x, q, scales, G))
+
+
+@pytest.mark.parametrize("G", [128])
+@pytest.mark.parametrize("M", [1, 4, 16])
+@pytest.mark.parametrize("N,K", DECODE_SHAPES[4:])
+def test_llama3_8b_shapes(M, N, K, G):
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales), ref_gemm(x, q, scales, G))
+
+
+# ---------------------------------------------------------------- prefill
+
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", PREFILL_M)
+@pytest.mark.parametrize("N,K", DECODE_SHAPES[:4])
+def test_prefill_auto(M, N, K, G):
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales), ref_gemm(x, q, scales, G))
+
+
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", [1, 3, 16, 17, 70, 200])
+@pytest.mark.parametrize("N,K", RAGGED)
+def test_ragged_shapes_auto(M, N, K, G):
+    if K % G:
+        pytest.skip("K must be a multiple of the group size")
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales), ref_gemm(x, q, scales, G))
+
+
+@pytest.mark.parametrize("variant", PREFILL_VARIANTS)
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", [1, 7, 16, 17, 33, 129])
+@pytest.mark.parametrize("N,K", [(64, 512), (208, 384), (512, 4096)])
+def test_forced_prefill_variants(variant, M, N, K, G):
+    if K % G:
+        pytest.skip("K must be a multiple of the group size")
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales, variant=variant), ref_gemm(x, q, scales, G))
+
+
+@pytest.mark.parametrize("G", GS)
+def test_prefill_variants_bitwise_equal(G):
+    """K is accumulated in one sequential order by every prefill config -> identical bits."""
+    x, q, scales, Wp = make_problem(200, 384, 2048, G, seed=5)
+    ys = [gemm(Wp, x, scales, variant=v) for v in PREFILL_VARIANTS]
+    for y in ys[1:]:
+        assert torch.equal(ys[0], y)
+
+
+@pytest.mark.parametrize("G", GS)
+def test_prefill_rows_independent_of_batch(G):
+    """Row i of the output must not depend on the other rows (padding rows included)."""
+    x, q, scales, Wp = make_problem(150, 256, 1024, G, seed=9)
+    full = gemm(Wp, x, scales)
+    for m in (17, 40, 64, 99):
+        assert torch.equal(gemm(Wp, x[:m].contiguous(), scales), full[:m])
+
+
+@pytest.mark.parametrize("G", [128])
+@pytest.mark.parametrize("M", [17, 128, 1024])
+@pytest.mark.parametrize("N,K", DECODE_SHAPES[4:7])
+def test_llama3_8b_prefill_shapes(M, N, K, G):
+    x, q, scales, Wp = make_problem(M, N, K, G)
+    assert_close(gemm(Wp, x, scales), ref_gemm(x, q, scales, G))
+
+
+def test_decode_variant_matches_prefill():
+    x, q, scales, Wp = make_problem(8, 1024, 2048, 128)
+    ref = ref_gemm(x, q, scales, 128)
+    assert_close(gemm(Wp, x, scales, variant=0), ref)
+    assert_close(gemm(Wp, x, scales, variant=3), ref)
+
+
+def test_decode_variant_rejects_unsupported_shapes():
+    x, q, scales, Wp = make_problem(32, 64, 512, 64)
+    with pytest.raises(RuntimeError, match="decode kernel needs"):
+        gemm(Wp, x, scales, variant=0)
+    x, q, scales, Wp = make_problem(4, 80, 640, 64)
+    with pytest.raises(RuntimeError, match="decode kernel needs"):
+        gemm(Wp, x, scales, variant=0)
+
+
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("scale_mode", ["tiny", "large", "mixed"])
+def test_hard_scale_and_activation_ranges(G, scale_mode):
+    M, N, K = 16, 256, 2048
+    x, q, scales, Wp = make_problem(M, N, K, G, seed=23)
+    if scale_mode == "tiny":
+        scales.fill_(2.0 ** -14)
+        x.mul_(128)
+    elif scale_mode == "large":
+        scales.fill_(16.0)
+        x.mul_(8)
+    else:
+        scales[:, ::2] = 2.0 ** -10
+        scales[:, 1::2] = 8.0
+        x[::2].mul_(0.125)
+        x[1::2].mul_(8)
+    ref = ref_gemm(x, q, scales, G)
+    for v in [-1, 0] + PREFILL_VARIANTS:
+        assert_close(gemm(Wp, x, scales, variant=v), ref, tol=4e-3)
+
+
+@pytest.mark.parametrize("G", GS)
+def test_onehot_k_mapping(G):
+    """x = e_k  ->  y must equal column k of the dequantised W exactly, in every K slice."""
+    N, K = 128, 1024
+    _, q, scales, Wp = make_problem(1, N, K, G)
+    Wd = torch.from_numpy(oracle.dequantize_w4(q.numpy(), to_np(scales), G)).cuda()
+    ks = [0, 1, 2, 7, 8, 15, 16, 17, 63, 64, 65, 127, 128, 255, 256, 511, 512, 513, 1022, 1023]
+    for i in range(0, len(ks), 16):
+        chunk = ks[i:i + 16]
+        x = torch.zeros(len(chunk), K, dtype=torch.half, device="cuda")
+        for m, k in enumerate(chunk):
+            x[m, k] = 1
+        for v in [-1, 0] + PREFILL_VARIANTS:
+            y = gemm(Wp, x, scales, variant=v)
+            assert torch.equal(y, Wd[:, chunk].t().contiguous()), f"k-mapping wrong for k in {chunk}, variant {v}"
+
+
+@pytest.mark.parametrize("fill", ["zeros", "fifteens", "random"])
+def test_nibble_extremes(fill):
+    from w4a16_opt import pack_int4
+    M, N, K, G = 4, 128, 1024, 64
+    gen = torch.Generator().manual_seed(1)
+    q = {"zeros": torch.zeros(N, K, dtype=torch.uint8),
+         "fifteens": torch.full((N, K), 15, dtype=torch.uint8),
+         "random": torch.randint(0, 16, (N, K), dtype=torch.uint8, generator=gen)}[fill]
+    scales = (torch.rand(K // G, N, generator=gen) * 0.05 + 0.001).half().cuda()
+    x = torch.randn(M, K, generator=gen).half().cuda()
+    Wp = pack_int4(q).cuda()
+    ref = ref_gemm(x, q, scales, G)
+    for v in [-1] + PREFILL_VARIANTS:
+        assert_close(gemm(Wp, x, scales, variant=v), ref)
+
+
+def test_zero_input():
+    x, q, scales, Wp = make_problem(5, 128, 1024, 64)
+    for v in [-1] + PREFILL_VARIANTS:
+        assert not gemm(Wp, torch.zeros_like(x), scales, variant=v).any()
+
+
+@pytest.mark.parametrize("M", [8, 300])
+def test_deterministic(M):
+    x, q, scales, Wp = make_problem(M, 1024, 2048, 128)
+    assert torch.equal(gemm(Wp, x, scales), gemm(Wp, x, scales))
+
+
+@pytest.mark.parametrize("M", [1, 12, 40, 300])
+def test_cuda_graph_capture(M):
+    """An inference engine calls this inside CUDA graphs."""
+    x, q, scales, Wp = make_problem(M, 512, 1024, 128)
+    gemm(Wp, x, scales)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        y = gemm(Wp, x, scales)
+    x2 = torch.randn_like(x)
+    x.copy_(x2)
+    g.replay()
+    torch.cuda.synchronize()
+    assert_close(y, ref_gemm(x2, q, scales, 128))
+
+
+def test_rejects_bad_inputs():
+    def args(**kw):
+        p = dict(M=2, N=64, K=512, G=64)
+        p.update(kw)
+        x, q, s, Wp = make_problem(p["M"], p["N"], p["K"], p["G"])
+        return Wp, x, s
+
+    Wp, x, s = args()
+    with pytest.raises(RuntimeError, match="fp16"):
+        gemm(Wp, x.float(), s)
+    with pytest.raises(RuntimeError, match="int32"):
+        gemm(Wp.to(torch.int64), x, s)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        gemm(Wp.cpu(), x.cpu(), s.cpu())
+    with pytest.raises(RuntimeError, match="contiguous"):
+        gemm(Wp, torch.empty(512, 2, dtype=torch.half, device="cuda").t(), s)
+    with pytest.raises(RuntimeError, match="variant"):
+        gemm(Wp, x, s, variant=7)
+    with pytest.raises(RuntimeError, match="multiple of 64"):
+        gemm(Wp[: 64 * 32 // 8], torch.zeros(2, 32, dtype=torch.half, device="cuda"), s[:1, :64].contiguous())
+    with pytest.raises(RuntimeError, match="multiple of 16"):
+        gemm(Wp[: 24 * 512 // 8], x, s[:, :24].contiguous())
+    with pytest.raises(RuntimeError, match="unsupported group size"):
+        gemm(*args(G=32))
+    with pytest.raises(RuntimeError, match="M must be at least 1"):
+        gemm(Wp, x[:0], s)
+
+
+# ---------------------------------------------------------------- golden vectors and BASELINE configs
+
+@pytest.mark.parametrize("base", sorted(k[:-2] for k in GOLDEN.files if k.startswith("gemm_") and k.endswith("_y")))
+def test_golden_vectors(base):
+    """Outputs of the reference's own ref_gemm on committed inputs."""
+    x = torch.from_numpy(GOLDEN[base + "_x"]).cuda()
+    Wp = torch.from_numpy(GOLDEN[base + "_wp"]).cuda()
+    s = torch.from_numpy(GOLDEN[base + "_scales"]).cuda()
+    for v in [-1] + PREFILL_VARIANTS:
+        assert_close(gemm(Wp, x, s, variant=v), GOLDEN[base + "_y"])
+
+
+def test_config0_against_reference_output():
+    """M=1, N=K=4096, G=128, seed 0 -- against the reference's fp32 output."""
+    x, q, s, Wp = make_workload(1, 4096, 4096, 128, seed=0)
+    assert_close(gemm(Wp, x, s), GOLDEN["cfg0_y"])
+
+
+@pytest.mark.parametrize("M", [1, 4, 8, 16])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (1024, 4096), (14336, 4096), (4096, 14336)])
+def test_config1_decode_sweep(M, N, K):
+    x, q, s, Wp = make_workload(M, N, K, 128, seed=1)
+    assert_close(gemm(Wp, x, s), ref_gemm(x, q, s, 128))
+
+
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", [128, 512, 2048, 8192])
+@pytest.mark.parametrize("N,K", [(14336, 4096), (4096, 14336)])
+def test_config2_prefill(M, N, K, G):
+    """Full-size prefill: rows are independent, so a seeded sample of 48 rows is
+    checked against the oracle, plus the row-sum checksum of the whole output."""
+    x, q, s, Wp = make_workload(M, N, K, G, seed=2)
+    y = gemm(Wp, x, s)
+    rows = np.sort(np.random.default_rng(M + N).choice(M, size=min(M, 48), replace=False))
+    assert_close(y[torch.from_numpy(rows).cuda()], ref_gemm(x, q, s, G, rows=rows))
+    # checksum of the full output: sum_n y[m, n] == x[m] . (sum_n W[n, :])
+    Wd_colsum = torch.from_numpy(oracle.dequantize_w4(q.numpy(), to_np(s), G).astype(np.float64).sum(0))
+    expect = x.double().cpu() @ Wd_colsum
+    got = y.double().sum(1).cpu()
+    err = (got - expect).abs().max().item() / expect.abs().max().item()
+    assert err < 2e-3, err
+
+
+@pytest.mark.parametrize("M", [1, 17, 37, 129])
+def test_config3_ragged(M):
+    x, q, s, Wp = make_workload(M, 4112, 4160, 64, seed=3)
+    assert_close(gemm(Wp, x, s), ref_gemm(x, q, s, 64))
+    for v in PREFILL_VARIANTS:
+        assert_close(gemm(Wp, x, s, variant=v), ref_gemm(x, q, s, 64))
+
+
+def test_config3_small():
+    x, q, s, Wp = make_workload(3, 1040, 2048, 128, seed=3)
+    for v in [-1, 0] + PREFILL_VARIANTS:
+        assert_close(gemm(Wp, x, s, variant=v), ref_gemm(x, q, s, 128))
+
+
+# ---------------------------------------------------------------- fp32 output, dequant, routing, C ABI
+
+@pytest.mark.parametrize("M", [1, 16, 200])
+@pytest.mark.parametrize("variant", [-1, 3])
+def test_fp32_output_mode(M, variant):
+    from w4a16_opt import w4a16_gemm_out
+    x, q, s, Wp = make_problem(M, 512, 2048, 128, seed=4)
+    if variant == 0 and M > 16:
+        pytest.skip("decode contract")
+    y = torch.empty(M, 512, dtype=torch.float32, device="cuda")
+    w4a16_gemm_out(Wp, x, s, y, variant=variant)
+    ref = ref_gemm(x, q, s, 128)
+    assert_close(y, ref)
+    # fp16 output is exactly the fp32 result rounded once
+    y16 = gemm(Wp, x, s, variant=variant)
+    assert torch.equal(y16, y.half())
+
+
+@pytest.mark.parametrize("N,K,G", [(64, 512, 64), (208, 384, 128), (4096, 4096, 128), (1040, 2048, 64)])
+def test_dequant_bit_exact(N, K, G):
+    from w4a16_opt import w4a16_dequant
+    _, q, s, Wp = make_problem(1, N, K, G, seed=6)
+    out = w4a16_dequant(Wp, s, K)
+    ref = oracle.dequantize_w4(q.numpy(), to_np(s), G)
+    assert np.array_equal(to_np(out).view(np.uint16), ref.view(np.uint16))
+
+
+def test_query_route():
+    from w4a16_opt import query_route
+    r = query_route(1, 4096, 4096, 32)
+    assert r["kernel"] == "decode" and r["grid"] >= 148
+    r = query_route(3, 4112, 4160, 65)
+    assert r["kernel"] == "decode"
+    r = query_route(2048, 14336, 4096, 32)
+    assert r["kernel"] == "prefill" and r["grid"] <= 148
+    for v in PREFILL_VARIANTS:
+        assert query_route(5, 4096, 4096, 32, v)["config"] == v
+    assert query_route(5, 4096, 4096, 32, 0)["kernel"] == "decode"
+
+
+@pytest.mark.parametrize("M", [3, 300])
+def test_c_abi_direct_call(M):
+    """Call libw4a16.so through ctypes with raw pointers; bitwise equal to the binding."""
+    from w4a16_opt import capi
+    lib = capi.load()
+    x, q, s, Wp = make_problem(M, 256, 1024, 64, seed=8)
+    y = torch.empty(M, 256, dtype=torch.half, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream
+    st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
+                        Wp.numel(), -1, capi.W4A16_OUT_F16, ctypes.c_void_p(stream))
+    capi.check(st, lib)
+    torch.cuda.synchronize()
+    assert torch.equal(y, gemm(Wp, x, s))
+    # a rejected call reports the reference's message through the ABI
+    st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
+                        Wp.numel(), 9, 0, ctypes.c_void_p(stream))
+    assert st == 2 and "variant" in capi.last_error(lib)
+
+
+def test_device_status_clean():
+    """No kernel in this session hit a bounded-wait timeout."""
+    from w4a16_opt import device_status
+    assert device_status() == 0

@@ -1,0 +1,205 @@
+// extern "C" entry points of libw4a16.so (declared in include/w4a16.h).
+//
+// Validation order and messages follow the reference's host entry
+// w4a16_gemm_cuda (src/vectorized/kernel.cu:218-249) so callers see the same
+// errors; tensor-level checks (CUDA residency, contiguity, dtypes, ranks) are
+// the torch shim's job because plain pointers carry none of that.
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <cstdlib>
+#include <cstring>
+#include <string>
+
+#include "../../include/w4a16.h"
+#include "internal.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+w4a16_status fail(w4a16_status s, const std::string& msg) {
+    g_last_error = msg;
+    return s;
+}
+
+w4a16_status ok() {
+    return W4A16_OK;
+}
+
+bool pdl_enabled() {
+    static const bool on = [] {
+        const char* v = std::getenv("W4A16_PDL");
+        return !(v && (std::strcmp(v, "0") == 0 || std::strcmp(v, "off") == 0));
+    }();
+    return on;
+}
+
+bool decode_contract(int64_t M, int64_t N, int64_t K) {
+    return M >= 1 && M <= 16 && N % 64 == 0 && K % 512 == 0;
+}
+
+w4a16_status check_device(w4a16::DeviceInfo* d) {
+    cudaError_t err = w4a16::device_info(d);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    if (d->cc_major != 10 || d->cc_minor != 0)
+        return fail(W4A16_ERR_DEVICE, "w4a16 kernels are built for sm_100a (B200); current device is sm_" +
+                                          std::to_string(d->cc_major) + std::to_string(d->cc_minor));
+    return ok();
+}
+
+struct Route {
+    bool decode;
+    w4a16::DecodePlan dp;
+    w4a16::PrefillPlan pp;
+};
+
+// Routing: the decode kernel serves every M <= 16 call under variant -1 (it
+// handles N % 16 and K % 64 tails, unlike the reference's decode kernel, whose
+// stricter contract kernel.cu:243 is still enforced for an explicit variant 0);
+// everything else goes to the tcgen05 prefill kernel.
+Route make_route(int M, int N, int K, int G, int variant, const w4a16::DeviceInfo& d) {
+    Route r{};
+    r.decode = (variant == 0) || (variant == -1 && M <= 16);
+    if (r.decode) {
+        r.dp = w4a16::plan_decode(M, N, K, G, d);
+        // A K slice too long for shared memory even at 16 splits: the prefill
+        // kernel streams K instead (same result within tolerance).
+        if (!r.dp.valid) r.decode = false;
+    }
+    if (!r.decode) r.pp = w4a16::plan_prefill(M, N, K, G, variant > 0 ? variant : 0, d);
+    return r;
+}
+
+}  // namespace
+
+extern "C" {
+
+int32_t w4a16_abi_version(void) {
+    return W4A16_ABI_VERSION;
+}
+
+w4a16_status w4a16_validate(const void* Wp, const void* x, const void* scales, int64_t M, int64_t N, int64_t K,
+                            int64_t groups, int64_t wp_words, int32_t variant) {
+    if (variant < -1 || variant > 4) return fail(W4A16_ERR_VARIANT, "variant must be -1 (auto), 0 (decode) or 1..4");
+    if (M < 1) return fail(W4A16_ERR_M, "M must be at least 1");
+    if (M >= (1LL << 31) || K >= (1LL << 31) || N >= (1LL << 31) || N < 0 || K < 0)
+        return fail(W4A16_ERR_DIM_RANGE, "dimensions must fit in int32");
+    if (K % 64 != 0) return fail(W4A16_ERR_K_MULTIPLE, "K must be a multiple of 64");
+    if (N % 16 != 0) return fail(W4A16_ERR_N_MULTIPLE, "N must be a multiple of 16");
+    if (groups <= 0 || K % groups != 0) return fail(W4A16_ERR_GROUPS, "K must be divisible by the number of groups");
+    if (wp_words != N * K / 8) return fail(W4A16_ERR_WP_SIZE, "Wp must hold N*K/8 words");
+    if ((Wp && reinterpret_cast<uintptr_t>(Wp) % 16) || (x && reinterpret_cast<uintptr_t>(x) % 16) ||
+        (scales && reinterpret_cast<uintptr_t>(scales) % 16))
+        return fail(W4A16_ERR_ALIGNMENT, "Wp, x and scales must be 16-byte aligned");
+    const int64_t G = K / groups;
+    if (G != 64 && G != 128)
+        return fail(W4A16_ERR_GROUP_SIZE, "unsupported group size " + std::to_string(G) + ", supported: 64, 128");
+    if (variant == 0 && !decode_contract(M, N, K))
+        return fail(W4A16_ERR_DECODE_SHAPE,
+                    "decode kernel needs M in [1, 16], N a multiple of 64 and K a multiple of 512 "
+                    "(use variant=-1 or 1..4 for other shapes)");
+    return ok();
+}
+
+w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
+                        int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
+                        void* stream) {
+    w4a16_status s = w4a16_validate(Wp, x, scales, M, N, K, groups, wp_words, variant);
+    if (s != W4A16_OK) return s;
+    if (!Wp || !x || !scales || !y) return fail(W4A16_ERR_NULL_POINTER, "Wp, x, scales and y must be non-null");
+    if (out_dtype != W4A16_OUT_F16 && out_dtype != W4A16_OUT_F32)
+        return fail(W4A16_ERR_OUT_DTYPE, "out_dtype must be 0 (fp16) or 1 (fp32)");
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    const int G = (int)(K / groups);
+    w4a16::GemmArgs a{Wp, x, scales, y, (int)M, (int)N, (int)K, G, out_dtype == W4A16_OUT_F32,
+                      static_cast<cudaStream_t>(stream), pdl_enabled()};
+    const Route r = make_route(a.M, a.N, a.K, G, variant, d);
+    cudaError_t err = r.decode ? w4a16::launch_decode(a, r.dp) : w4a16::launch_prefill(a, r.pp);
+    if (err == cudaSuccess) err = cudaGetLastError();
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, int32_t variant, w4a16_route* out) {
+    w4a16_status s = w4a16_validate(nullptr, nullptr, nullptr, M, N, K, groups, N * K / 8, variant);
+    if (s != W4A16_OK) return s;
+    if (!out) return fail(W4A16_ERR_NULL_POINTER, "out must be non-null");
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    const Route r = make_route((int)M, (int)N, (int)K, (int)(K / groups), variant, d);
+    std::memset(out, 0, sizeof(*out));
+    if (r.decode) {
+        out->kernel = 0;
+        out->config = 0;
+        out->tile_m = r.dp.mt * 8;
+        out->tile_n = 64;
+        out->split_k = r.dp.split;
+        out->grid = r.dp.grid_x * r.dp.split;
+        out->stages = 4;
+        out->smem_bytes = (int32_t)r.dp.smem;
+    } else {
+        out->kernel = 1;
+        out->config = r.pp.config;
+        out->tile_m = r.pp.tok;
+        out->tile_n = 128;
+        out->split_k = 1;
+        out->grid = r.pp.grid;
+        out->stages = r.pp.stages;
+        out->smem_bytes = (int32_t)r.pp.smem;
+    }
+    return ok();
+}
+
+w4a16_status w4a16_dequant(const int32_t* Wp, const void* scales, void* out, int64_t N, int64_t K, int64_t groups,
+                           void* stream) {
+    w4a16_status s = w4a16_validate(Wp, nullptr, scales, 1, N, K, groups, N * K / 8, -1);
+    if (s != W4A16_OK) return s;
+    if (!Wp || !scales || !out) return fail(W4A16_ERR_NULL_POINTER, "Wp, scales and out must be non-null");
+    if (reinterpret_cast<uintptr_t>(out) % 4) return fail(W4A16_ERR_ALIGNMENT, "out must be 4-byte aligned");
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    cudaError_t err = w4a16::launch_dequant(Wp, scales, out, (int)N, (int)K, (int)(K / groups),
+                                            static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_device_status(int32_t* code, int32_t reset) {
+    if (!code) return fail(W4A16_ERR_NULL_POINTER, "code must be non-null");
+    int c = 0;
+    cudaError_t err = w4a16::read_device_status(&c, reset != 0);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    *code = c;
+    if (c != 0) return fail(W4A16_ERR_DEVICE_TIMEOUT, "a kernel wait timed out (device status " + std::to_string(c) + ")");
+    return ok();
+}
+
+const char* w4a16_status_string(w4a16_status status) {
+    switch (status) {
+        case W4A16_OK: return "W4A16_OK";
+        case W4A16_ERR_NULL_POINTER: return "W4A16_ERR_NULL_POINTER";
+        case W4A16_ERR_VARIANT: return "W4A16_ERR_VARIANT";
+        case W4A16_ERR_M: return "W4A16_ERR_M";
+        case W4A16_ERR_DIM_RANGE: return "W4A16_ERR_DIM_RANGE";
+        case W4A16_ERR_K_MULTIPLE: return "W4A16_ERR_K_MULTIPLE";
+        case W4A16_ERR_N_MULTIPLE: return "W4A16_ERR_N_MULTIPLE";
+        case W4A16_ERR_GROUPS: return "W4A16_ERR_GROUPS";
+        case W4A16_ERR_WP_SIZE: return "W4A16_ERR_WP_SIZE";
+        case W4A16_ERR_ALIGNMENT: return "W4A16_ERR_ALIGNMENT";
+        case W4A16_ERR_GROUP_SIZE: return "W4A16_ERR_GROUP_SIZE";
+        case W4A16_ERR_DECODE_SHAPE: return "W4A16_ERR_DECODE_SHAPE";
+        case W4A16_ERR_OUT_DTYPE: return "W4A16_ERR_OUT_DTYPE";
+        case W4A16_ERR_DEVICE: return "W4A16_ERR_DEVICE";
+        case W4A16_ERR_CUDA: return "W4A16_ERR_CUDA";
+        case W4A16_ERR_DEVICE_TIMEOUT: return "W4A16_ERR_DEVICE_TIMEOUT";
+    }
+    return "W4A16_ERR_UNKNOWN";
+}
+
+const char* w4a16_last_error(void) {
+    return g_last_error.c_str();
+}
+
+}  // extern "C"

@@ -1,0 +1,73 @@
+// Host-side interfaces shared by the C-ABI launcher and the kernel translation units.
+#pragma once
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace w4a16 {
+
+// One validated GEMM call: y[M, N] = x[M, K] @ W^T, W from packed nibbles + fp16 scales.
+struct GemmArgs {
+    const void* wp;       // int32 [N*K/8] packed nibbles (fragment order)
+    const void* x;        // fp16 [M, K]
+    const void* scales;   // fp16 [K/G, N]
+    void* y;              // fp16 or fp32 [M, N]
+    int M, N, K, G;
+    bool out_f32;         // fp32 output (tensor-parallel partials) instead of fp16
+    cudaStream_t stream;
+    bool pdl;             // launch with programmatic dependent launch enabled
+};
+
+struct DeviceInfo {
+    int device;
+    int num_sms;
+    int max_smem_optin;
+    int cc_major, cc_minor;
+};
+
+// Cached properties of the current device (thread-safe).
+cudaError_t device_info(DeviceInfo* out);
+
+// Raise a kernel's dynamic shared-memory cap to the device opt-in maximum, once
+// per (kernel, device) (thread-safe).
+cudaError_t ensure_max_dynamic_smem(const void* func);
+
+// Allow clusters of more than 8 CTAs for a kernel (once per kernel and device).
+cudaError_t ensure_nonportable_cluster(const void* func);
+
+// Read (and optionally clear) the device status word that bounded waits set on
+// timeout.  Synchronises with the device.
+cudaError_t read_device_status(int* code, bool reset);
+
+// ---------------------------------------------------------------- decode (M <= 16)
+struct DecodePlan {
+    int split;      // K splits = CTAs per cluster
+    int kc_per;     // 64-wide K chunks per split
+    int grid_x;     // CTAs along N (4 n16 blocks each)
+    int mt;         // 8-token tiles (1: M <= 8, 2: M <= 16)
+    size_t smem;    // dynamic shared memory bytes
+    bool valid;     // false if no split up to 16 fits the K slice in shared memory
+};
+DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);
+cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p);
+
+// ---------------------------------------------------------------- prefill (any M)
+struct PrefillPlan {
+    int config;     // 1..4
+    int tok;        // token tile (UMMA N): 32, 64, 128 or 256
+    int stages;     // shared-memory pipeline depth
+    int a_stages;   // TMEM A-operand ring depth
+    int accs;       // TMEM accumulator buffers
+    int tiles;      // total output tiles
+    int grid;       // persistent CTAs
+    size_t smem;
+};
+// config 1..4 forces a token tile (32 / 64 / 128 / 256); 0 = choose from the shape.
+PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInfo& dev);
+cudaError_t launch_prefill(const GemmArgs& a, const PrefillPlan& p);
+
+// ---------------------------------------------------------------- debug dequant
+cudaError_t launch_dequant(const void* wp, const void* scales, void* out, int N, int K, int G,
+                           cudaStream_t stream);
+
+}  // namespace w4a16

@@ -1,0 +1,126 @@
+// The single device-code translation unit: decode, prefill and dequant kernels,
+// the device status word, and the host helpers they need (device properties,
+// shared-memory opt-in, TMA tensor maps).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <mutex>
+#include <set>
+#include <utility>
+
+#include "internal.h"
+#include "ptx.cuh"
+#include "decode.cuh"
+#include "prefill.cuh"
+#include "dequant_kernel.cuh"
+
+namespace w4a16 {
+
+cudaError_t device_info(DeviceInfo* out) {
+    static std::mutex mu;
+    static DeviceInfo cache[64];
+    static bool have[64] = {};
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev < 0 || dev >= 64) return cudaErrorInvalidDevice;
+    std::lock_guard<std::mutex> lk(mu);
+    if (!have[dev]) {
+        DeviceInfo d;
+        d.device = dev;
+        if ((err = cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev)) != cudaSuccess) return err;
+        if ((err = cudaDeviceGetAttribute(&d.max_smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev)) != cudaSuccess) return err;
+        if ((err = cudaDeviceGetAttribute(&d.cc_major, cudaDevAttrComputeCapabilityMajor, dev)) != cudaSuccess) return err;
+        if ((err = cudaDeviceGetAttribute(&d.cc_minor, cudaDevAttrComputeCapabilityMinor, dev)) != cudaSuccess) return err;
+        cache[dev] = d;
+        have[dev] = true;
+    }
+    *out = cache[dev];
+    return cudaSuccess;
+}
+
+cudaError_t ensure_max_dynamic_smem(const void* func) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    DeviceInfo d;
+    cudaError_t err = device_info(&d);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({func, d.device})) return cudaSuccess;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin);
+    if (err == cudaSuccess) done.insert({func, d.device});
+    return err;
+}
+
+cudaError_t ensure_nonportable_cluster(const void* func) {
+    static std::mutex mu;
+    static std::set<std::pair<const void*, int>> done;
+    DeviceInfo d;
+    cudaError_t err = device_info(&d);
+    if (err != cudaSuccess) return err;
+    std::lock_guard<std::mutex> lk(mu);
+    if (done.count({func, d.device})) return cudaSuccess;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+    if (err == cudaSuccess) done.insert({func, d.device});
+    return err;
+}
+
+cudaError_t read_device_status(int* code, bool reset) {
+    cudaError_t err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) return err;
+    err = cudaMemcpyFromSymbol(code, w4a16_device_status, sizeof(int));
+    if (err != cudaSuccess || !reset) return err;
+    const int zero = 0;
+    return cudaMemcpyToSymbol(w4a16_device_status, &zero, sizeof(int));
+}
+
+static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx, CUtensorMap* tw, CUtensorMap* ts) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return cudaErrorNotSupported;
+    const cuuint32_t one[3] = {1, 1, 1};
+    {   // x [M, K] fp16, box {64, tok}, 128-byte swizzle (one swizzle atom per row)
+        const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)tok};
+        if (encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {   // packed words viewed as [NB][KC][128] int32, box {128, 1, 8}
+        const cuuint64_t dims[3] = {128, (cuuint64_t)(a.K / 64), (cuuint64_t)(a.N / 16)};
+        const cuuint64_t strides[2] = {512, (cuuint64_t)(a.K / 64) * 512};
+        const cuuint32_t box[3] = {128, 1, 8};
+        if (encode(tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<void*>(a.wp), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {   // scales [K/G, N] fp16, box {128, 1}
+        const cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)(a.K / a.G)};
+        const cuuint64_t strides[1] = {(cuuint64_t)a.N * 2};
+        const cuuint32_t box[2] = {128, 1};
+        if (encode(ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.scales), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
+}  // namespace w4a16

@@ -1,0 +1,349 @@
+// Prefill path (any M): persistent, warp-specialised tcgen05 GEMM.
+// Included by the single device-code translation unit (kernels.cu) only.
+//
+// Replaces the reference's mma.sync prefill kernel (src/vectorized/prefill.cuh:27-184)
+// and its config machinery (kernel.cu:56-214).  The contraction is
+//
+//     D[n, tok] (TMEM, fp32) += Wdeq[n, k] (A, TMEM, fp16) * x[tok, k] (B, smem, fp16)
+//
+// i.e. the weights are the UMMA M side (128 output channels per tile) and the
+// tokens the UMMA N side (TOK = 32..256 per tile).  The dequantised weights
+// never touch shared memory: each dequant warp turns its lanes' packed words
+// into m16n8k16 A fragments with the exact fp16 dequant and writes them into a
+// TMEM ring with tcgen05.st.16x128b, whose register-to-(lane, column) map is
+// exactly that fragment order.  Shared memory only carries the TMA-loaded x
+// tile (128-byte swizzle), the raw packed words and one scale row per stage.
+//
+// Warp roles (448 threads, one CTA per SM, all 512 TMEM columns):
+//   warp 0      TMA producer: x tile [TOK x 64] (SW128), packed words of 8 n16
+//               blocks for one 64-wide K chunk (3-D tensor map), 128 scales
+//   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
+//   warps 2-9   dequant: warp w owns n16 block 2*(w%4) + (w>=6) of the tile,
+//               i.e. TMEM lanes inside its own lane quarter
+//   warps 10-13 epilogue: tcgen05.ld of the accumulator, fp16/fp32 stores
+//
+// K is walked in one sequential order for every tile shape, so all prefill
+// configs (TOK = 32/64/128/256) give bit-identical results and a row's output
+// does not depend on the other rows of the batch.
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include <algorithm>
+#include <cmath>
+
+#include "dequant.cuh"
+#include "internal.h"
+#include "ptx.cuh"
+
+namespace w4a16 {
+
+constexpr int kPfThreads = 14 * 32;
+constexpr int kPfRows = 128;                 // output channels per tile (UMMA M)
+constexpr int kPfWBytes = 8 * 512;           // packed words: 8 n16 blocks x one 64-k chunk
+constexpr int kPfSBytes = kPfRows * 2;       // one fp16 scale row slice
+constexpr int kPfSmemBudget = 227 * 1024;    // opt-in dynamic shared memory per CTA on sm_100
+
+template <int TOK>
+struct PfCfg {
+    static_assert(TOK == 32 || TOK == 64 || TOK == 128 || TOK == 256, "token tile");
+    static constexpr int X_BYTES = TOK * 128;                         // TOK rows x 64 fp16
+    static constexpr int STAGE = (X_BYTES + kPfWBytes + kPfSBytes + 1023) / 1024 * 1024;
+    static constexpr int ACCS = TOK <= 128 ? 2 : 1;                   // TMEM accumulator buffers
+    static constexpr int A_COL0 = ACCS * TOK;                         // first A-ring column
+    static constexpr int A_STAGES = (512 - A_COL0) / 32 < 8 ? (512 - A_COL0) / 32 : 8;
+    static constexpr int BAR_BYTES = 1024;
+    static constexpr int ST_FIT = (kPfSmemBudget - 1024 - BAR_BYTES) / STAGE;
+    static constexpr int STAGES = ST_FIT < 12 ? ST_FIT : 12;
+    static constexpr int SMEM_USED = 1024 /*alignment slack*/ + STAGES * STAGE + BAR_BYTES;
+    // Request > half of the SM's shared memory so at most one CTA (which owns all
+    // 512 TMEM columns) is ever resident on an SM.
+    static constexpr int SMEM = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
+    static_assert(A_COL0 + A_STAGES * 32 <= 512, "TMEM budget");
+    static_assert(STAGES >= 3, "pipeline depth");
+};
+
+// UMMA instruction descriptor, kind::f16: fp16 A/B, fp32 D, both K-major, M=128, N=TOK.
+template <int TOK>
+__host__ __device__ constexpr uint32_t pf_idesc() {
+    return (1u << 4)                         // D format f32
+         | (0u << 7) | (0u << 10)            // A, B format f16
+         | ((uint32_t)(TOK >> 3) << 17)      // N >> 3
+         | ((uint32_t)(kPfRows >> 4) << 24); // M >> 4
+}
+
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row groups 1024 B apart.
+__device__ __forceinline__ uint64_t pf_sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr >> 4) & 0x3FFF)
+         | ((uint64_t)1 << 16)               // leading byte offset (unused for swizzled K-major)
+         | ((uint64_t)(1024 >> 4) << 32)     // stride byte offset
+         | ((uint64_t)1 << 46)               // descriptor version (sm_100)
+         | ((uint64_t)2 << 61);              // SWIZZLE_128B
+}
+
+template <int G, int TOK, bool OUT_F32>
+__global__ void __launch_bounds__(kPfThreads, 1)
+prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+               const __grid_constant__ CUtensorMap tm_s, void* __restrict__ yv, int M, int N, int K)
+{
+    using C = PfCfg<TOK>;
+    constexpr int ST = C::STAGES, NA = C::A_STAGES, NACC = C::ACCS;
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw = smem_u32(smem_raw);
+    const uint32_t base = (raw + 1023u) & ~1023u;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+    const uint32_t bar0 = base + ST * C::STAGE;
+    auto full = [&](int s) { return bar0 + 8u * s; };
+    auto empty = [&](int s) { return bar0 + 8u * (ST + s); };
+    auto afull = [&](int a) { return bar0 + 8u * (2 * ST + a); };
+    auto aempty = [&](int a) { return bar0 + 8u * (2 * ST + NA + a); };
+    auto accfull = [&](int b) { return bar0 + 8u * (2 * ST + 2 * NA + b); };
+    auto accempty = [&](int b) { return bar0 + 8u * (2 * ST + 2 * NA + NACC + b); };
+    const uint32_t done_bar = bar0 + 8u * (2 * ST + 2 * NA + 2 * NACC);
+    const uint32_t tmem_slot = done_bar + 8u;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(full(s), 1);
+            mbar_init(empty(s), 8 * 32 + 1);   // every dequant lane + the MMA commit
+        }
+        for (int a = 0; a < NA; ++a) {
+            mbar_init(afull(a), 8 * 32);
+            mbar_init(aempty(a), 1);
+        }
+        for (int b = 0; b < NACC; ++b) {
+            mbar_init(accfull(b), 1);
+            mbar_init(accempty(b), 4 * 32);
+        }
+        mbar_init(done_bar, 1);
+        fence_mbar_init();
+        prefetch_tmap(&tm_x);
+        prefetch_tmap(&tm_w);
+        prefetch_tmap(&tm_s);
+    }
+    if (warp == 1) {
+        tmem_alloc(tmem_slot, 512);
+        tmem_relinquish();
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(smem_raw + (tmem_slot - raw));
+
+    pdl_wait();               // x is produced by the previous kernel; y may still be read by it
+    pdl_launch_dependents();
+
+    const int n_tiles = (N + kPfRows - 1) / kPfRows;
+    const int total = n_tiles * ((M + TOK - 1) / TOK);
+    const int KT = K >> 6;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            int it = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+                const int tt = tile / n_tiles, tn = tile % n_tiles;
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST;
+                    if (!mbar_wait(empty(s), ((it / ST) & 1) ^ 1, kDevTimeoutPipeline)) { ok = false; break; }
+                    const uint32_t sb = base + s * C::STAGE;
+                    mbar_arrive_expect_tx(full(s), C::X_BYTES + kPfWBytes + kPfSBytes);
+                    tma_load_2d(sb, &tm_x, kt * 64, tt * TOK, full(s));
+                    tma_load_3d(sb + C::X_BYTES, &tm_w, 0, kt, tn * 8, full(s));
+                    tma_load_2d(sb + C::X_BYTES + kPfWBytes, &tm_s, tn * kPfRows, (kt * 64) / G, full(s));
+                }
+            }
+            if (!ok) {
+                // Error path: the last ST issued stages may still be landing.
+                for (int j = max(0, it - ST); j < it; ++j)
+                    mbar_wait(full(j % ST), (j / ST) & 1, kDevTimeoutDrain);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            constexpr uint32_t idesc = pf_idesc<TOK>();
+            int it = 0, tc = 0;
+            bool ok = true;
+            for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x, ++tc) {
+                const int b = tc % NACC;
+                if (!mbar_wait(accempty(b), ((tc / NACC) & 1) ^ 1, kDevTimeoutPipeline)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t d = tmem + (uint32_t)(b * TOK);
+                for (int kt = 0; kt < KT; ++kt, ++it) {
+                    const int s = it % ST, a = it % NA;
+                    if (!mbar_wait(full(s), (it / ST) & 1, kDevTimeoutPipeline) ||
+                        !mbar_wait(afull(a), (it / NA) & 1, kDevTimeoutPipeline)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint32_t xa = base + s * C::STAGE;
+                    const uint32_t at = tmem + (uint32_t)(C::A_COL0 + a * 32);
+#pragma unroll
+                    for (int k16 = 0; k16 < 4; ++k16)
+                        tc_mma_ts(d, at + k16 * 8, pf_sw128_desc(xa + k16 * 32), idesc, (kt | k16) != 0);
+                    tc_commit(empty(s));
+                    tc_commit(aempty(a));
+                }
+                if (ok) tc_commit(accfull(b));
+            }
+            tc_commit(done_bar);   // every MMA of this CTA retired before TMEM is released
+            mbar_wait(done_bar, 0, kDevTimeoutDrain);
+        }
+    } else if (warp < 10) {
+        // ------------------------------------------------------------ dequant -> TMEM A ring
+        const int nbl = 2 * (warp & 3) + (warp >= 6 ? 1 : 0);   // n16 block inside the tile
+        const int g = lane >> 2;
+        const uint32_t lane_field = (uint32_t)(16 * nbl) << 16;
+        int it = 0;
+        bool ok = true;
+        for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
+            for (int kt = 0; kt < KT; ++kt, ++it) {
+                const int s = it % ST, a = it % NA;
+                bool w_ok = mbar_wait(full(s), (it / ST) & 1, kDevTimeoutPipeline);
+                w_ok = w_ok && mbar_wait(aempty(a), ((it / NA) & 1) ^ 1, kDevTimeoutPipeline);
+                if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
+                tc_fence_after();
+                const uint32_t sb = base + s * C::STAGE + C::X_BYTES;
+                const uint4 w = lds128(sb + nbl * 512 + lane * 16);
+                const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem_raw + (sb + kPfWBytes - raw));
+                const uint32_t s_lo = bcast_half(sc[nbl * 16 + g]);
+                const uint32_t s_hi = bcast_half(sc[nbl * 16 + g + 8]);
+                uint32_t r[16];
+                dequant_word(w.x, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[0]));
+                dequant_word(w.y, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[4]));
+                dequant_word(w.z, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[8]));
+                dequant_word(w.w, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[12]));
+                mbar_arrive(empty(s));   // this lane is done with the stage's packed words and scales
+                tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * 32), r);
+                tc_wait_st();
+                tc_fence_before();
+                mbar_arrive(afull(a));
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int q = warp & 3;
+        const uint32_t lane_field = (uint32_t)(32 * q) << 16;
+        int tc = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tc) {
+            const int tt = tile / n_tiles, tn = tile % n_tiles;
+            const int b = tc % NACC;
+            if (!__all_sync(0xffffffffu, mbar_wait(accfull(b), (tc / NACC) & 1, kDevTimeoutPipeline))) break;
+            tc_fence_after();
+            const int n = tn * kPfRows + 32 * q + lane;
+            const int tok0 = tt * TOK;
+#pragma unroll 1
+            for (int c0 = 0; c0 < TOK && tok0 + c0 < M; c0 += 32) {
+                uint32_t r[32];
+                tmem_ld_32x32b_x32(tmem + lane_field + (uint32_t)(b * TOK + c0), r);
+                tc_wait_ld();
+                if (n < N) {
+                    const int jmax = min(32, M - (tok0 + c0));
+                    if (OUT_F32) {
+                        float* y = static_cast<float*>(yv) + (size_t)(tok0 + c0) * N + n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < jmax) y[(size_t)j * N] = __uint_as_float(r[j]);
+                    } else {
+                        __half* y = static_cast<__half*>(yv) + (size_t)(tok0 + c0) * N + n;
+#pragma unroll
+                        for (int j = 0; j < 32; ++j)
+                            if (j < jmax) y[(size_t)j * N] = __float2half_rn(__uint_as_float(r[j]));
+                    }
+                }
+            }
+            tc_fence_before();
+            mbar_arrive(accempty(b));
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+// ------------------------------------------------------------------ host side
+inline int pf_tok_of_config(int config) {
+    switch (config) {
+        case 1: return 32;
+        case 2: return 64;
+        case 3: return 128;
+        default: return 256;
+    }
+}
+
+PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInfo& dev) {
+    (void)K; (void)G;
+    const int n_tiles = (N + kPfRows - 1) / kPfRows;
+    if (config < 1 || config > 4) {
+        // Wave-quantised cost of the MMA work; below TOK ~ 96 the per-k-step
+        // dequant (fixed 128 x 64 weights) rather than the MMA sets the pace.
+        double best = 1e300;
+        config = 3;
+        for (int c = 4; c >= 1; --c) {
+            const int tok = pf_tok_of_config(c);
+            const double tiles = (double)n_tiles * ((M + tok - 1) / tok);
+            const double waves = std::ceil(tiles / dev.num_sms);
+            const double cost = waves * std::max(tok, 96);
+            if (cost < best - 1e-9) { best = cost; config = c; }
+        }
+    }
+    PrefillPlan p;
+    p.config = config;
+    p.tok = pf_tok_of_config(config);
+    switch (p.tok) {
+        case 32:  p.stages = PfCfg<32>::STAGES;  p.a_stages = PfCfg<32>::A_STAGES;  p.accs = PfCfg<32>::ACCS;  p.smem = PfCfg<32>::SMEM;  break;
+        case 64:  p.stages = PfCfg<64>::STAGES;  p.a_stages = PfCfg<64>::A_STAGES;  p.accs = PfCfg<64>::ACCS;  p.smem = PfCfg<64>::SMEM;  break;
+        case 128: p.stages = PfCfg<128>::STAGES; p.a_stages = PfCfg<128>::A_STAGES; p.accs = PfCfg<128>::ACCS; p.smem = PfCfg<128>::SMEM; break;
+        default:  p.stages = PfCfg<256>::STAGES; p.a_stages = PfCfg<256>::A_STAGES; p.accs = PfCfg<256>::ACCS; p.smem = PfCfg<256>::SMEM; break;
+    }
+    p.tiles = n_tiles * ((M + p.tok - 1) / p.tok);
+    p.grid = std::min(p.tiles, dev.num_sms);
+    return p;
+}
+
+// Tensor maps for one call.  x: [M, K] fp16, box {64, TOK}, 128-byte swizzle.
+// Packed words as [NB][KC][128] int32, box {128, 1, 8} (8 n16 blocks of one chunk).
+// Scales: [K/G, N] fp16, box {128, 1}.  Out-of-range boxes read as zero.
+cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx, CUtensorMap* tw, CUtensorMap* ts);
+
+template <int G, int TOK, bool F32>
+static cudaError_t launch_prefill_t(const GemmArgs& a, const PrefillPlan& p) {
+    CUtensorMap tx, tw, ts;
+    cudaError_t err = make_prefill_tensor_maps(a, TOK, &tx, &tw, &ts);
+    if (err != cudaSuccess) return err;
+    auto kern = prefill_kernel<G, TOK, F32>;
+    err = ensure_max_dynamic_smem(reinterpret_cast<const void*>(kern));
+    if (err != cudaSuccess) return err;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(p.grid, 1, 1);
+    cfg.blockDim = dim3(kPfThreads, 1, 1);
+    cfg.dynamicSmemBytes = PfCfg<TOK>::SMEM;
+    cfg.stream = a.stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = a.pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, tx, tw, ts, a.y, a.M, a.N, a.K);
+}
+
+template <int G, bool F32>
+static cudaError_t launch_prefill_g(const GemmArgs& a, const PrefillPlan& p) {
+    switch (p.tok) {
+        case 32:  return launch_prefill_t<G, 32, F32>(a, p);
+        case 64:  return launch_prefill_t<G, 64, F32>(a, p);
+        case 128: return launch_prefill_t<G, 128, F32>(a, p);
+        default:  return launch_prefill_t<G, 256, F32>(a, p);
+    }
+}
+
+cudaError_t launch_prefill(const GemmArgs& a, const PrefillPlan& p) {
+    if (a.G == 64) return a.out_f32 ? launch_prefill_g<64, true>(a, p) : launch_prefill_g<64, false>(a, p);
+    return a.out_f32 ? launch_prefill_g<128, true>(a, p) : launch_prefill_g<128, false>(a, p);
+}
+
+}  // namespace w4a16

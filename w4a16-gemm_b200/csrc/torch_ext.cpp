@@ -1,0 +1,122 @@
+// Thin PyTorch binding over the C ABI (include/w4a16.h), module w4a16_opt._C.
+//
+// Keeps the reference's Python surface -- w4a16_gemm(Wp, x, scales, variant=-1)
+// (src/vectorized/extension.cpp:5-8) -- and its tensor checks, in the same
+// order and with the same messages (src/vectorized/kernel.cu:219-223); every
+// other check and the launch happen behind the C ABI.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <climits>
+
+#include "../../include/w4a16.h"
+
+namespace {
+
+void check(w4a16_status s) {
+    TORCH_CHECK(s == W4A16_OK, w4a16_last_error());
+}
+
+int32_t clamp_variant(int64_t v) {
+    return (v < -1 || v > 4) ? INT32_MAX : (int32_t)v;   // out of range -> rejected by w4a16_validate
+}
+
+void check_tensors(const torch::Tensor& Wp, const torch::Tensor& x, const torch::Tensor& scales) {
+    TORCH_CHECK(Wp.is_cuda() && x.is_cuda() && scales.is_cuda(), "all tensors must be CUDA");
+    TORCH_CHECK(Wp.is_contiguous() && x.is_contiguous() && scales.is_contiguous(), "contiguous only");
+    TORCH_CHECK(Wp.dtype() == torch::kInt32, "Wp must be int32");
+    TORCH_CHECK(x.dtype() == torch::kHalf && scales.dtype() == torch::kHalf, "x, scales must be fp16");
+    TORCH_CHECK(x.dim() == 2 && scales.dim() == 2, "x must be [M, K], scales must be [K/G, N]");
+    TORCH_CHECK(Wp.device() == x.device() && scales.device() == x.device(), "all tensors must be on one device");
+}
+
+void run(const torch::Tensor& Wp, const torch::Tensor& x, const torch::Tensor& scales, torch::Tensor& y,
+         int32_t variant) {
+    const at::cuda::CUDAGuard guard(x.device());
+    auto stream = at::cuda::getCurrentCUDAStream();
+    check(w4a16_gemm(Wp.data_ptr<int32_t>(), x.data_ptr(), scales.data_ptr(), y.data_ptr(), x.size(0),
+                     scales.size(1), x.size(1), scales.size(0), Wp.numel(), variant,
+                     y.scalar_type() == torch::kFloat ? W4A16_OUT_F32 : W4A16_OUT_F16, stream.stream()));
+}
+
+}  // namespace
+
+// y = x @ W^T, fresh fp16 [M, N] output (reference: kernel.cu:218-267).
+torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, int64_t variant) {
+    check_tensors(Wp, x, scales);
+    const int32_t v = clamp_variant(variant);
+    check(w4a16_validate(Wp.data_ptr(), x.data_ptr(), scales.data_ptr(), x.size(0), scales.size(1), x.size(1),
+                         scales.size(0), Wp.numel(), v));
+    auto y = torch::empty({x.size(0), scales.size(1)}, x.options());
+    run(Wp, x, scales, y, v);
+    return y;
+}
+
+// Same GEMM into a caller-provided contiguous y: fp16, or fp32 for row-parallel partial sums.
+torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, torch::Tensor y,
+                                int64_t variant) {
+    check_tensors(Wp, x, scales);
+    TORCH_CHECK(y.is_cuda() && y.device() == x.device(), "y must be a CUDA tensor on x's device");
+    TORCH_CHECK(y.is_contiguous(), "contiguous only");
+    TORCH_CHECK(y.dtype() == torch::kHalf || y.dtype() == torch::kFloat, "y must be fp16 or fp32");
+    TORCH_CHECK(y.dim() == 2 && y.size(0) == x.size(0) && y.size(1) == scales.size(1), "y must be [M, N]");
+    const int32_t v = clamp_variant(variant);
+    check(w4a16_validate(Wp.data_ptr(), x.data_ptr(), scales.data_ptr(), x.size(0), scales.size(1), x.size(1),
+                         scales.size(0), Wp.numel(), v));
+    run(Wp, x, scales, y, v);
+    return y;
+}
+
+// Dequantised weights fp16 [N, K] (debug / verification).
+torch::Tensor w4a16_dequant_py(torch::Tensor Wp, torch::Tensor scales, int64_t K) {
+    TORCH_CHECK(Wp.is_cuda() && scales.is_cuda(), "all tensors must be CUDA");
+    TORCH_CHECK(Wp.is_contiguous() && scales.is_contiguous(), "contiguous only");
+    TORCH_CHECK(Wp.dtype() == torch::kInt32, "Wp must be int32");
+    TORCH_CHECK(scales.dtype() == torch::kHalf && scales.dim() == 2, "scales must be fp16 [K/G, N]");
+    const at::cuda::CUDAGuard guard(Wp.device());
+    const int64_t N = scales.size(1);
+    auto out = torch::empty({N, K}, scales.options());
+    check(w4a16_validate(Wp.data_ptr(), nullptr, scales.data_ptr(), 1, N, K, scales.size(0), Wp.numel(), -1));
+    check(w4a16_dequant(Wp.data_ptr<int32_t>(), scales.data_ptr(), out.data_ptr(), N, K, scales.size(0),
+                        at::cuda::getCurrentCUDAStream().stream()));
+    return out;
+}
+
+pybind11::dict query_route_py(int64_t M, int64_t N, int64_t K, int64_t groups, int64_t variant) {
+    w4a16_route r;
+    check(w4a16_query_route(M, N, K, groups, clamp_variant(variant), &r));
+    pybind11::dict d;
+    d["kernel"] = r.kernel == 0 ? "decode" : "prefill";
+    d["config"] = r.config;
+    d["tile_m"] = r.tile_m;
+    d["tile_n"] = r.tile_n;
+    d["split_k"] = r.split_k;
+    d["grid"] = r.grid;
+    d["stages"] = r.stages;
+    d["smem_bytes"] = r.smem_bytes;
+    return d;
+}
+
+int64_t device_status_py(bool reset) {
+    int32_t code = 0;
+    w4a16_status s = w4a16_device_status(&code, reset ? 1 : 0);
+    TORCH_CHECK(s == W4A16_OK || s == W4A16_ERR_DEVICE_TIMEOUT, w4a16_last_error());
+    return code;
+}
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+    m.def("w4a16_gemm", &w4a16_gemm_py,
+          "W4A16 GEMM on B200: decode (M <= 16) weight-streaming kernel + tcgen05 prefill for any M",
+          pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("variant") = -1);
+    m.def("w4a16_gemm_out", &w4a16_gemm_out_py, "W4A16 GEMM into a preallocated fp16/fp32 output",
+          pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("y"),
+          pybind11::arg("variant") = -1);
+    m.def("w4a16_dequant", &w4a16_dequant_py, "dequantised fp16 [N, K] weights", pybind11::arg("Wp"),
+          pybind11::arg("scales"), pybind11::arg("K"));
+    m.def("query_route", &query_route_py, "kernel / tile / grid the GEMM would launch", pybind11::arg("M"),
+          pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("groups"), pybind11::arg("variant") = -1);
+    m.def("device_status", &device_status_py, "device status word set by timed-out kernel waits",
+          pybind11::arg("reset") = false);
+    m.attr("ABI_VERSION") = w4a16_abi_version();
+}

@@ -1,0 +1,114 @@
+"""Tensor-parallel W4A16 projections over torch.distributed (NCCL on B200s).
+
+The packed format shards without repacking along N and with one slice along K:
+
+* Column-parallel (q/k/v/gate/up): rank r owns n16 blocks
+  [r*NB/P, (r+1)*NB/P) -- a contiguous slab of the packed words viewed as
+  [NB, KC, 32, 4] -- and scales[:, n-slice].  Each rank computes y_r [M, N/P];
+  an all-gather over NVLink assembles y [M, N].
+* Row-parallel (o/down): rank r owns 64-wide K chunks [r*KC/P, (r+1)*KC/P)
+  (``[:, kslice]`` of the same view, copied once at load) and scales[g-slice, :].
+  Each rank multiplies its K slice of x into an fp32 partial [M, N]; an fp32
+  all-reduce sums the partials and one cast gives fp16 y.
+
+The reference has no distributed code; this layer follows the sharding the
+north-star configuration asks for (Llama-3-70B gate/up split along N, down
+split along K).  The GEMM itself is always the CUDA kernel; ``gemm_out`` is
+injectable only so the host-side sharding logic can be exercised on CPU
+process groups in tests.
+"""
+from __future__ import annotations
+
+from typing import Callable, Optional
+
+import torch
+import torch.distributed as dist
+
+GemmOut = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+def _default_gemm_out(Wp, x, scales, y):
+    from . import w4a16_gemm_out
+    return w4a16_gemm_out(Wp, x, scales, y)
+
+
+def shard_columns(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int, world: int):
+    """(Wp_r, scales_r) for rank r of a column-parallel split of N."""
+    NB, KC = N // 16, K // 64
+    if NB % world:
+        raise ValueError(f"N/16 = {NB} n16 blocks do not split evenly over {world} ranks")
+    nb = NB // world
+    Wp_r = Wp.view(NB, KC, 32, 4)[rank * nb:(rank + 1) * nb].contiguous().view(-1)
+    s_r = scales[:, rank * nb * 16:(rank + 1) * nb * 16].contiguous()
+    return Wp_r, s_r
+
+
+def shard_rows(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int, world: int):
+    """(Wp_r, scales_r) for rank r of a row-parallel split of K."""
+    NB, KC = N // 16, K // 64
+    G = K // scales.shape[0]
+    if KC % world or (K // world) % G:
+        raise ValueError(f"K = {K} does not split into {world} slices of whole 64-chunks and {G}-groups")
+    kc = KC // world
+    Wp_r = Wp.view(NB, KC, 32, 4)[:, rank * kc:(rank + 1) * kc].contiguous().view(-1)
+    gpr = (K // world) // G
+    s_r = scales[rank * gpr:(rank + 1) * gpr].contiguous()
+    return Wp_r, s_r
+
+
+class ColumnParallelW4A16:
+    """y = x @ W^T with W split along N over the process group; returns full y [M, N]."""
+
+    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.N, self.K = N, K
+        self.N_local = N // self.world
+        self.Wp, self.scales = shard_columns(Wp, scales, N, K, self.rank, self.world)
+        self.gemm_out = gemm_out or _default_gemm_out
+
+    def local(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        y = out if out is not None else torch.empty(x.shape[0], self.N_local, dtype=torch.float16, device=x.device)
+        return self.gemm_out(self.Wp, x, self.scales, y)
+
+    def gather(self, y_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        M = y_local.shape[0]
+        buf = torch.empty(self.world, M, self.N_local, dtype=y_local.dtype, device=y_local.device)
+        dist.all_gather_into_tensor(buf, y_local.contiguous(), group=self.group)
+        if M == 1:
+            return buf.view(1, self.N)
+        y = out if out is not None else torch.empty(M, self.N, dtype=y_local.dtype, device=y_local.device)
+        y.view(M, self.world, self.N_local).copy_(buf.permute(1, 0, 2))
+        return y
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        return self.gather(self.local(x))
+
+
+class RowParallelW4A16:
+    """y = x @ W^T with W split along K; the caller passes this rank's K slice of x."""
+
+    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.N, self.K = N, K
+        self.K_local = K // self.world
+        self.Wp, self.scales = shard_rows(Wp, scales, N, K, self.rank, self.world)
+        self.gemm_out = gemm_out or _default_gemm_out
+
+    def x_slice(self, x: torch.Tensor) -> torch.Tensor:
+        return x[:, self.rank * self.K_local:(self.rank + 1) * self.K_local].contiguous()
+
+    def partial(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        y = out if out is not None else torch.empty(x_local.shape[0], self.N, dtype=torch.float32,
+                                                    device=x_local.device)
+        return self.gemm_out(self.Wp, x_local, self.scales, y)
+
+    def reduce(self, partial: torch.Tensor) -> torch.Tensor:
+        dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
+        return partial.half()
+
+    def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
+        return self.reduce(self.partial(x_local))
