@@ -259,12 +259,20 @@ def run_ours(args):
             step_bytes += alg_bytes(M, N, K, DECODE_G)
             in_bytes += 2 * M * K
             out_bytes += 2 * M * N
+    # one zero-filled workspace shared by every GEMM of the step (they run in stream order)
+    ws = w4a16_opt.make_workspace(max(w4a16_opt.workspace_bytes(u["M"], u["N"] // (world if "y_local" in u else 1),
+                                                                u["K"] // (world if "x_local" in u else 1),
+                                                                (u["K"] // (world if "x_local" in u else 1)) // DECODE_G)
+                                      for u in units))
+    for u in units:
+        if "layer" in u:
+            u["layer"].workspace = ws
     torch.cuda.synchronize()
 
     def step():
         for u in units:
             if world == 1:
-                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"])
+                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws)
             elif "x_local" in u:
                 u["layer"].partial(u["x_local"], out=u["part"])
                 u["layer"].reduce(u["part"])
@@ -328,7 +336,7 @@ def run_ours(args):
 
         def pstep():
             for Wp, x, s, y in punits:
-                w4a16_opt.w4a16_gemm_out(Wp, x, s, y)
+                w4a16_opt.w4a16_gemm_out(Wp, x, s, y, workspace=ws)
 
         psteps = max(3, args.prefill_steps)
         pms = graph_time_ms(pstep, psteps, 3, world)

@@ -15,6 +15,14 @@
  * from w4a16_last_error().  No function allocates device memory, so GEMM
  * launches may be captured in CUDA graphs.
  *
+ * Workspace: the decode path (M <= 16) splits K across SMs and combines the
+ * split partial sums through a caller-provided device workspace of
+ * w4a16_workspace_bytes() bytes (256-byte aligned).  It must be zero-filled
+ * before its first use; every completed call leaves the counter words it uses
+ * at zero again (the rest is scratch), so one workspace serves any number of
+ * calls, of any shapes, issued in stream order.  Calls that may run
+ * concurrently need separate workspaces.
+ *
  * This header replaces the reference's torch-typed entry point
  *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)
  * (akshay919191/W4A16-GEMM src/vectorized/kernel.cu:218, bound as
@@ -48,7 +56,8 @@ typedef enum w4a16_status {
     W4A16_ERR_OUT_DTYPE = 12,        /* out_dtype is not a w4a16_out_dtype value */
     W4A16_ERR_DEVICE = 13,           /* current device is not an sm_100 GPU */
     W4A16_ERR_CUDA = 14,             /* a CUDA runtime / driver call failed */
-    W4A16_ERR_DEVICE_TIMEOUT = 15    /* a kernel's bounded wait ran out (see w4a16_device_status) */
+    W4A16_ERR_DEVICE_TIMEOUT = 15,   /* a kernel's bounded wait ran out (see w4a16_device_status) */
+    W4A16_ERR_WORKSPACE = 16         /* workspace missing, too small or misaligned */
 } w4a16_status;
 
 typedef enum w4a16_out_dtype {
@@ -61,10 +70,11 @@ typedef struct w4a16_route {
     int32_t config;     /* prefill tile config 1..4 (token tile 32/64/128/256); 0 for decode */
     int32_t tile_m;     /* tokens per tile (decode: 8 or 16 padded rows) */
     int32_t tile_n;     /* output channels per tile (decode 64, prefill 128) */
-    int32_t split_k;    /* K splits (decode cluster size; 1 for prefill) */
+    int32_t split_k;    /* decode: stream-K work units (64 columns x 256 K); prefill: 1 */
     int32_t grid;       /* CTAs launched */
     int32_t stages;     /* pipeline depth */
     int32_t smem_bytes; /* dynamic shared memory per CTA */
+    uint64_t workspace_bytes; /* workspace the call needs (see w4a16_workspace_bytes) */
 } w4a16_route;
 
 /* Version of this ABI (W4A16_ABI_VERSION). */
@@ -79,13 +89,18 @@ w4a16_status w4a16_validate(const void* Wp, const void* x, const void* scales,
                             int64_t M, int64_t N, int64_t K, int64_t groups,
                             int64_t wp_words, int32_t variant);
 
+/* Bytes of workspace w4a16_gemm needs for this call (0 if none). */
+w4a16_status w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t groups, int32_t variant,
+                                   uint64_t* bytes);
+
 /* y = x @ W^T on `stream`.  variant: -1 auto, 0 decode kernel (reference decode
  * contract: M <= 16, N % 64 == 0, K % 512 == 0), 1..4 force a prefill tile
  * config.  out_dtype selects fp16 or fp32 y.  Replaces w4a16_gemm_cuda
- * (kernel.cu:218-267); unlike it, y is caller-allocated. */
+ * (kernel.cu:218-267); unlike it, y and the workspace are caller-allocated. */
 w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y,
                         int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
-                        int32_t variant, int32_t out_dtype, void* stream);
+                        int32_t variant, int32_t out_dtype, void* workspace, uint64_t workspace_bytes,
+                        void* stream);
 
 /* The launch w4a16_gemm would make for this call (kernel choice, tiles, grid).
  * Mirrors the reference's routing (kernel.cu:242-249) and prefill config

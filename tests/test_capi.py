@@ -86,14 +86,14 @@ def test_validate_accepts(kw):
 
 def test_gemm_null_pointers_rejected():
     lib = capi.load()
-    st = lib.w4a16_gemm(None, None, None, None, 2, 64, 512, 8, 64 * 512 // 8, -1, 0, None)
+    st = lib.w4a16_gemm(None, None, None, None, 2, 64, 512, 8, 64 * 512 // 8, -1, 0, None, 0, None)
     assert st == 1 and "non-null" in capi.last_error(lib)
 
 
 def test_gemm_bad_out_dtype_rejected():
     lib = capi.load()
     p = ctypes.c_void_p(0x10000)
-    st = lib.w4a16_gemm(p, p, p, p, 2, 64, 512, 8, 64 * 512 // 8, -1, 5, None)
+    st = lib.w4a16_gemm(p, p, p, p, 2, 64, 512, 8, 64 * 512 // 8, -1, 5, None, 0, None)
     assert st == 12
 
 

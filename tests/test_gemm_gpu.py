@@ -294,9 +294,13 @@ def test_config3_ragged(M):
 
 
 def test_config3_small():
+    """M=3, N=1040 (not a multiple of 64), K=2048: auto routes to the decode kernel,
+    variant 0 is rejected (reference decode contract), every prefill config is exact."""
     x, q, s, Wp = make_workload(3, 1040, 2048, 128, seed=3)
-    for v in [-1, 0] + PREFILL_VARIANTS:
+    for v in [-1] + PREFILL_VARIANTS:
         assert_close(gemm(Wp, x, s, variant=v), ref_gemm(x, q, s, 128))
+    with pytest.raises(RuntimeError, match="decode kernel needs"):
+        gemm(Wp, x, s, variant=0)
 
 
 # ---------------------------------------------------------------- fp32 output, dequant, routing, C ABI
@@ -329,7 +333,8 @@ def test_dequant_bit_exact(N, K, G):
 def test_query_route():
     from w4a16_opt import query_route
     r = query_route(1, 4096, 4096, 32)
-    assert r["kernel"] == "decode" and r["grid"] >= 148
+    assert r["kernel"] == "decode" and r["grid"] == torch.cuda.get_device_properties(0).multi_processor_count
+    assert r["workspace_bytes"] > 0
     r = query_route(3, 4112, 4160, 65)
     assert r["kernel"] == "decode"
     r = query_route(2048, 14336, 4096, 32)
@@ -347,15 +352,36 @@ def test_c_abi_direct_call(M):
     x, q, s, Wp = make_problem(M, 256, 1024, 64, seed=8)
     y = torch.empty(M, 256, dtype=torch.half, device="cuda")
     stream = torch.cuda.current_stream().cuda_stream
-    st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
-                        Wp.numel(), -1, capi.W4A16_OUT_F16, ctypes.c_void_p(stream))
-    capi.check(st, lib)
-    torch.cuda.synchronize()
-    assert torch.equal(y, gemm(Wp, x, s))
+    nbytes = ctypes.c_uint64(0)
+    capi.check(lib.w4a16_workspace_bytes(M, 256, 1024, 16, -1, ctypes.byref(nbytes)), lib)
+    ws = torch.zeros(max(1, nbytes.value), dtype=torch.uint8, device="cuda")
+    for _ in range(2):   # the workspace is left zeroed: a second call reuses it
+        st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
+                            Wp.numel(), -1, capi.W4A16_OUT_F16, ws.data_ptr(), nbytes.value, ctypes.c_void_p(stream))
+        capi.check(st, lib)
+        torch.cuda.synchronize()
+        assert torch.equal(y, gemm(Wp, x, s))
     # a rejected call reports the reference's message through the ABI
     st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
-                        Wp.numel(), 9, 0, ctypes.c_void_p(stream))
+                        Wp.numel(), 9, 0, ws.data_ptr(), nbytes.value, ctypes.c_void_p(stream))
     assert st == 2 and "variant" in capi.last_error(lib)
+    if nbytes.value:
+        st = lib.w4a16_gemm(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, 256, 1024, 16,
+                            Wp.numel(), -1, 0, None, 0, ctypes.c_void_p(stream))
+        assert st == 16 and "workspace" in capi.last_error(lib)
+
+
+def test_shared_workspace_across_shapes():
+    """One workspace serves calls of different shapes in any order (decode stream-K counters)."""
+    from w4a16_opt import make_workspace, w4a16_gemm_out, workspace_bytes
+    shapes = [(1, 4096, 4096), (16, 14336, 4096), (3, 1024, 4096), (8, 28672, 4096), (1, 256, 2048), (5, 4096, 14336)]
+    ws = make_workspace(max(workspace_bytes(M, N, K, K // 128) for M, N, K in shapes))
+    for rep in range(2):
+        for i, (M, N, K) in enumerate(shapes):
+            x, q, s, Wp = make_workload(M, N, K, 128, seed=40 + i)
+            y = torch.empty(M, N, dtype=torch.half, device="cuda")
+            w4a16_gemm_out(Wp, x, s, y, workspace=ws)
+            assert_close(y, ref_gemm(x, q, s, 128))
 
 
 def test_device_status_clean():

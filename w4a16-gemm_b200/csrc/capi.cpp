@@ -71,6 +71,10 @@ Route make_route(int M, int N, int K, int G, int variant, const w4a16::DeviceInf
     return r;
 }
 
+size_t route_workspace(const Route& r) {
+    return r.decode ? r.dp.workspace : 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -104,7 +108,7 @@ w4a16_status w4a16_validate(const void* Wp, const void* x, const void* scales, i
 
 w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
                         int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
-                        void* stream) {
+                        void* workspace, uint64_t workspace_bytes, void* stream) {
     w4a16_status s = w4a16_validate(Wp, x, scales, M, N, K, groups, wp_words, variant);
     if (s != W4A16_OK) return s;
     if (!Wp || !x || !scales || !y) return fail(W4A16_ERR_NULL_POINTER, "Wp, x, scales and y must be non-null");
@@ -114,8 +118,16 @@ w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, vo
     if ((s = check_device(&d)) != W4A16_OK) return s;
     const int G = (int)(K / groups);
     w4a16::GemmArgs a{Wp, x, scales, y, (int)M, (int)N, (int)K, G, out_dtype == W4A16_OUT_F32,
-                      static_cast<cudaStream_t>(stream), pdl_enabled()};
+                      static_cast<cudaStream_t>(stream), pdl_enabled(), workspace, (size_t)workspace_bytes};
     const Route r = make_route(a.M, a.N, a.K, G, variant, d);
+    const size_t need = route_workspace(r);
+    if (need > 0) {
+        if (!workspace) return fail(W4A16_ERR_WORKSPACE, "this call needs a workspace of " + std::to_string(need) + " bytes");
+        if (workspace_bytes < need)
+            return fail(W4A16_ERR_WORKSPACE, "workspace too small: " + std::to_string(workspace_bytes) + " < " +
+                                                 std::to_string(need) + " bytes");
+        if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(W4A16_ERR_WORKSPACE, "workspace must be 256-byte aligned");
+    }
     cudaError_t err = r.decode ? w4a16::launch_decode(a, r.dp) : w4a16::launch_prefill(a, r.pp);
     if (err == cudaSuccess) err = cudaGetLastError();
     if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
@@ -130,14 +142,15 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
     if ((s = check_device(&d)) != W4A16_OK) return s;
     const Route r = make_route((int)M, (int)N, (int)K, (int)(K / groups), variant, d);
     std::memset(out, 0, sizeof(*out));
+    out->workspace_bytes = route_workspace(r);
     if (r.decode) {
         out->kernel = 0;
         out->config = 0;
         out->tile_m = r.dp.mt * 8;
         out->tile_n = 64;
-        out->split_k = r.dp.split;
-        out->grid = r.dp.grid_x * r.dp.split;
-        out->stages = 4;
+        out->split_k = r.dp.units;
+        out->grid = r.dp.ctas;
+        out->stages = r.dp.stages;
         out->smem_bytes = (int32_t)r.dp.smem;
     } else {
         out->kernel = 1;
@@ -149,6 +162,17 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
         out->stages = r.pp.stages;
         out->smem_bytes = (int32_t)r.pp.smem;
     }
+    return ok();
+}
+
+w4a16_status w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t groups, int32_t variant,
+                                   uint64_t* bytes) {
+    w4a16_status s = w4a16_validate(nullptr, nullptr, nullptr, M, N, K, groups, N * K / 8, variant);
+    if (s != W4A16_OK) return s;
+    if (!bytes) return fail(W4A16_ERR_NULL_POINTER, "bytes must be non-null");
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    *bytes = route_workspace(make_route((int)M, (int)N, (int)K, (int)(K / groups), variant, d));
     return ok();
 }
 
@@ -194,6 +218,7 @@ const char* w4a16_status_string(w4a16_status status) {
         case W4A16_ERR_DEVICE: return "W4A16_ERR_DEVICE";
         case W4A16_ERR_CUDA: return "W4A16_ERR_CUDA";
         case W4A16_ERR_DEVICE_TIMEOUT: return "W4A16_ERR_DEVICE_TIMEOUT";
+        case W4A16_ERR_WORKSPACE: return "W4A16_ERR_WORKSPACE";
     }
     return "W4A16_ERR_UNKNOWN";
 }

@@ -16,6 +16,8 @@ struct GemmArgs {
     bool out_f32;         // fp32 output (tensor-parallel partials) instead of fp16
     cudaStream_t stream;
     bool pdl;             // launch with programmatic dependent launch enabled
+    void* workspace;      // zero-initialised before first use; left zeroed by every call
+    size_t workspace_bytes;
 };
 
 struct DeviceInfo {
@@ -41,15 +43,17 @@ cudaError_t read_device_status(int* code, bool reset);
 
 // ---------------------------------------------------------------- decode (M <= 16)
 struct DecodePlan {
-    int split;      // K splits = CTAs per cluster
-    int kc_per;     // 64-wide K chunks per split
-    int grid_x;     // CTAs along N (4 n16 blocks each)
-    int mt;         // 8-token tiles (1: M <= 8, 2: M <= 16)
-    size_t smem;    // dynamic shared memory bytes
-    bool valid;     // false if no split up to 16 fits the K slice in shared memory
+    int mt;           // 8-token tiles (1: M <= 8, 2: M <= 16)
+    int ctas;         // persistent CTAs (one per SM)
+    int units;        // stream-K work units (64 columns x 256 K each)
+    int stages;       // TMA ring depth
+    size_t smem;      // dynamic shared memory bytes
+    size_t workspace; // bytes of workspace the launch needs
+    bool valid;
 };
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p);
+size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev);
 
 // ---------------------------------------------------------------- prefill (any M)
 struct PrefillPlan {

@@ -197,8 +197,24 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
         :: "r"(dst), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
 
+// Pull a line into L2 (no register result): hides DRAM latency of a later load.
+__device__ __forceinline__ void prefetch_l2(const void* p) {
+    asm volatile("prefetch.global.L2::evict_last [%0];" :: "l"(p));
+}
+
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
+}
+
+// 16-byte async copy global -> shared (L2 only), and an mbarrier arrival that
+// fires once all of this thread's earlier cp.async copies have landed (the
+// barrier's expected count must include these arrivals: .noinc).
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
+}
+
+__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
+    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(bar) : "memory");
 }
 
 // ------------------------------------------------------------------ PDL

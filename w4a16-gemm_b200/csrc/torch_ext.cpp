@@ -9,6 +9,9 @@
 #include <torch/extension.h>
 
 #include <climits>
+#include <map>
+#include <mutex>
+#include <utility>
 
 #include "../../include/w4a16.h"
 
@@ -31,13 +34,44 @@ void check_tensors(const torch::Tensor& Wp, const torch::Tensor& x, const torch:
     TORCH_CHECK(Wp.device() == x.device() && scales.device() == x.device(), "all tensors must be on one device");
 }
 
+// Workspace for the stream-K decode path: one zero-filled buffer per (device,
+// stream), reused by every call on that stream (calls on one stream never
+// overlap, and each completed call leaves the buffer zeroed again).  While the
+// stream is being captured into a CUDA graph a fresh zero-filled buffer is
+// taken from the graph's pool instead, so the zero-fill is part of the graph.
+torch::Tensor workspace_for(const torch::Tensor& x, uint64_t bytes, cudaStream_t stream) {
+    if (bytes == 0) return torch::Tensor();
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    TORCH_CHECK(cudaStreamIsCapturing(stream, &cap) == cudaSuccess, "cudaStreamIsCapturing failed");
+    auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(x.device());
+    if (cap != cudaStreamCaptureStatusNone) return torch::zeros({(int64_t)bytes}, opts);
+    static std::mutex mu;
+    static std::map<std::pair<int, cudaStream_t>, torch::Tensor> cache;
+    std::lock_guard<std::mutex> lk(mu);
+    auto& ws = cache[{x.get_device(), stream}];
+    if (!ws.defined() || (uint64_t)ws.numel() < bytes) ws = torch::zeros({(int64_t)bytes}, opts);
+    return ws;
+}
+
 void run(const torch::Tensor& Wp, const torch::Tensor& x, const torch::Tensor& scales, torch::Tensor& y,
-         int32_t variant) {
+         int32_t variant, const c10::optional<torch::Tensor>& user_ws = c10::nullopt) {
     const at::cuda::CUDAGuard guard(x.device());
-    auto stream = at::cuda::getCurrentCUDAStream();
+    cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+    uint64_t ws_bytes = 0;
+    check(w4a16_workspace_bytes(x.size(0), scales.size(1), x.size(1), scales.size(0), variant, &ws_bytes));
+    torch::Tensor ws;
+    if (user_ws.has_value() && user_ws->defined()) {
+        ws = *user_ws;
+        TORCH_CHECK(ws.is_cuda() && ws.device() == x.device() && ws.is_contiguous(),
+                    "workspace must be a contiguous CUDA tensor on x's device");
+        ws_bytes = (uint64_t)ws.numel() * ws.element_size();
+    } else {
+        ws = workspace_for(x, ws_bytes, stream);
+    }
     check(w4a16_gemm(Wp.data_ptr<int32_t>(), x.data_ptr(), scales.data_ptr(), y.data_ptr(), x.size(0),
                      scales.size(1), x.size(1), scales.size(0), Wp.numel(), variant,
-                     y.scalar_type() == torch::kFloat ? W4A16_OUT_F32 : W4A16_OUT_F16, stream.stream()));
+                     y.scalar_type() == torch::kFloat ? W4A16_OUT_F32 : W4A16_OUT_F16,
+                     ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, stream));
 }
 
 }  // namespace
@@ -54,8 +88,10 @@ torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor sca
 }
 
 // Same GEMM into a caller-provided contiguous y: fp16, or fp32 for row-parallel partial sums.
+// `workspace` (optional): a zero-filled CUDA buffer of >= workspace_bytes(...) bytes that the
+// caller keeps for calls issued in stream order; otherwise the binding supplies one.
 torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, torch::Tensor y,
-                                int64_t variant) {
+                                int64_t variant, c10::optional<torch::Tensor> workspace) {
     check_tensors(Wp, x, scales);
     TORCH_CHECK(y.is_cuda() && y.device() == x.device(), "y must be a CUDA tensor on x's device");
     TORCH_CHECK(y.is_contiguous(), "contiguous only");
@@ -64,8 +100,14 @@ torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor
     const int32_t v = clamp_variant(variant);
     check(w4a16_validate(Wp.data_ptr(), x.data_ptr(), scales.data_ptr(), x.size(0), scales.size(1), x.size(1),
                          scales.size(0), Wp.numel(), v));
-    run(Wp, x, scales, y, v);
+    run(Wp, x, scales, y, v, workspace);
     return y;
+}
+
+int64_t workspace_bytes_py(int64_t M, int64_t N, int64_t K, int64_t groups, int64_t variant) {
+    uint64_t b = 0;
+    check(w4a16_workspace_bytes(M, N, K, groups, clamp_variant(variant), &b));
+    return (int64_t)b;
 }
 
 // Dequantised weights fp16 [N, K] (debug / verification).
@@ -95,6 +137,7 @@ pybind11::dict query_route_py(int64_t M, int64_t N, int64_t K, int64_t groups, i
     d["grid"] = r.grid;
     d["stages"] = r.stages;
     d["smem_bytes"] = r.smem_bytes;
+    d["workspace_bytes"] = r.workspace_bytes;
     return d;
 }
 
@@ -111,6 +154,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("variant") = -1);
     m.def("w4a16_gemm_out", &w4a16_gemm_out_py, "W4A16 GEMM into a preallocated fp16/fp32 output",
           pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("y"),
+          pybind11::arg("variant") = -1, pybind11::arg("workspace") = pybind11::none());
+    m.def("workspace_bytes", &workspace_bytes_py, "workspace bytes a GEMM call needs on the current device",
+          pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("groups"),
           pybind11::arg("variant") = -1);
     m.def("w4a16_dequant", &w4a16_dequant_py, "dequantised fp16 [N, K] weights", pybind11::arg("Wp"),
           pybind11::arg("scales"), pybind11::arg("K"));

@@ -46,9 +46,25 @@ def w4a16_gemm(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, variant:
 
 
 def w4a16_gemm_out(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, y: torch.Tensor,
-                   variant: int = -1) -> torch.Tensor:
-    """Same GEMM into a preallocated contiguous ``y`` (fp16, or fp32 for partial sums)."""
-    return _C.w4a16_gemm_out(Wp, x, scales, y, variant)
+                   variant: int = -1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """Same GEMM into a preallocated contiguous ``y`` (fp16, or fp32 for partial sums).
+
+    ``workspace``: optional CUDA buffer, zero-filled once (see ``make_workspace``) and then
+    reused by calls issued in stream order; every call leaves its counter words at zero.
+    Without it the binding keeps one per (device, stream), or zero-fills a fresh one
+    under graph capture.
+    """
+    return _C.w4a16_gemm_out(Wp, x, scales, y, variant, workspace)
+
+
+def workspace_bytes(M: int, N: int, K: int, groups: int, variant: int = -1) -> int:
+    """Workspace bytes a call with these dimensions needs on the current device."""
+    return _C.workspace_bytes(M, N, K, groups, variant)
+
+
+def make_workspace(nbytes: int, device=None) -> torch.Tensor:
+    """A zero-filled workspace buffer of at least ``nbytes`` bytes."""
+    return torch.zeros(max(256, int(nbytes)), dtype=torch.uint8, device=device or "cuda")
 
 
 def w4a16_dequant(Wp: torch.Tensor, scales: torch.Tensor, K: int) -> torch.Tensor:
@@ -68,6 +84,7 @@ def device_status(reset: bool = False) -> int:
 
 __all__ = [
     "w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status",
+    "workspace_bytes", "make_workspace",
     "pack_int4", "unpack_int4", "quantize_w4", "dequantize_w4",
     "LIBRARY_PATH", "ABI_VERSION", "PREFILL_VARIANTS",
 ]

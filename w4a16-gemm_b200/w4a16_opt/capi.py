@@ -2,7 +2,7 @@
 
     lib = load()                         # libw4a16.so next to this file
     st = lib.w4a16_gemm(Wp_ptr, x_ptr, s_ptr, y_ptr, M, N, K, groups, wp_words,
-                        variant, W4A16_OUT_F16, stream_ptr)
+                        variant, W4A16_OUT_F16, ws_ptr, ws_bytes, stream_ptr)
 
 Every exported function and its argument types are declared here; the
 ``EXPORTS`` table is the list include/w4a16.h declares.
@@ -21,22 +21,24 @@ STATUS_NAMES = {
     4: "W4A16_ERR_DIM_RANGE", 5: "W4A16_ERR_K_MULTIPLE", 6: "W4A16_ERR_N_MULTIPLE", 7: "W4A16_ERR_GROUPS",
     8: "W4A16_ERR_WP_SIZE", 9: "W4A16_ERR_ALIGNMENT", 10: "W4A16_ERR_GROUP_SIZE",
     11: "W4A16_ERR_DECODE_SHAPE", 12: "W4A16_ERR_OUT_DTYPE", 13: "W4A16_ERR_DEVICE", 14: "W4A16_ERR_CUDA",
-    15: "W4A16_ERR_DEVICE_TIMEOUT",
+    15: "W4A16_ERR_DEVICE_TIMEOUT", 16: "W4A16_ERR_WORKSPACE",
 }
 
 
 class Route(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in
-                ("kernel", "config", "tile_m", "tile_n", "split_k", "grid", "stages", "smem_bytes")]
+                ("kernel", "config", "tile_m", "tile_n", "split_k", "grid", "stages", "smem_bytes")] + \
+               [("workspace_bytes", ctypes.c_uint64)]
 
 
-_i64, _i32, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_void_p
+_i64, _i32, _u64, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p
 
 # name -> (restype, argtypes), one entry per declaration in include/w4a16.h
 EXPORTS = {
     "w4a16_abi_version": (_i32, []),
     "w4a16_validate": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32]),
-    "w4a16_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
+    "w4a16_workspace_bytes": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)]),
+    "w4a16_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp, _u64, _vp]),
     "w4a16_query_route": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(Route)]),
     "w4a16_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "w4a16_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),

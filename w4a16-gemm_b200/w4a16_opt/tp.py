@@ -27,9 +27,9 @@ import torch.distributed as dist
 GemmOut = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
 
 
-def _default_gemm_out(Wp, x, scales, y):
+def _default_gemm_out(Wp, x, scales, y, workspace=None):
     from . import w4a16_gemm_out
-    return w4a16_gemm_out(Wp, x, scales, y)
+    return w4a16_gemm_out(Wp, x, scales, y, workspace=workspace)
 
 
 def shard_columns(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int, world: int):
@@ -67,9 +67,15 @@ class ColumnParallelW4A16:
         self.N_local = N // self.world
         self.Wp, self.scales = shard_columns(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
+        self.workspace: Optional[torch.Tensor] = None   # optional zero-filled GEMM workspace
 
     def local(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         y = out if out is not None else torch.empty(x.shape[0], self.N_local, dtype=torch.float16, device=x.device)
+        return self._gemm(x, y)
+
+    def _gemm(self, x, y):
+        if self.workspace is not None:
+            return self.gemm_out(self.Wp, x, self.scales, y, workspace=self.workspace)
         return self.gemm_out(self.Wp, x, self.scales, y)
 
     def gather(self, y_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
@@ -97,6 +103,7 @@ class RowParallelW4A16:
         self.K_local = K // self.world
         self.Wp, self.scales = shard_rows(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
+        self.workspace: Optional[torch.Tensor] = None   # optional zero-filled GEMM workspace
 
     def x_slice(self, x: torch.Tensor) -> torch.Tensor:
         return x[:, self.rank * self.K_local:(self.rank + 1) * self.K_local].contiguous()
@@ -104,6 +111,8 @@ class RowParallelW4A16:
     def partial(self, x_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         y = out if out is not None else torch.empty(x_local.shape[0], self.N, dtype=torch.float32,
                                                     device=x_local.device)
+        if self.workspace is not None:
+            return self.gemm_out(self.Wp, x_local, self.scales, y, workspace=self.workspace)
         return self.gemm_out(self.Wp, x_local, self.scales, y)
 
     def reduce(self, partial: torch.Tensor) -> torch.Tensor:
