@@ -259,7 +259,7 @@ def run_ours(args):
             step_bytes += alg_bytes(M, N, K, DECODE_G)
             in_bytes += 2 * M * K
             out_bytes += 2 * M * N
-    # one zero-filled workspace shared by every GEMM of the step (they run in stream order)
+    # one workspace shared by every GEMM of the step (they run in stream order)
     ws = w4a16_opt.make_workspace(max(w4a16_opt.workspace_bytes(u["M"], u["N"] // (world if "y_local" in u else 1),
                                                                 u["K"] // (world if "x_local" in u else 1),
                                                                 (u["K"] // (world if "x_local" in u else 1)) // DECODE_G)

@@ -17,11 +17,10 @@
  *
  * Workspace: the decode path (M <= 16) splits K across SMs and combines the
  * split partial sums through a caller-provided device workspace of
- * w4a16_workspace_bytes() bytes (256-byte aligned).  It must be zero-filled
- * before its first use; every completed call leaves the counter words it uses
- * at zero again (the rest is scratch), so one workspace serves any number of
- * calls, of any shapes, issued in stream order.  Calls that may run
- * concurrently need separate workspaces.
+ * w4a16_workspace_bytes() bytes (256-byte aligned).  It is scratch: a call
+ * writes every byte it later reads, so it needs no initialisation, and one
+ * workspace serves any number of calls, of any shapes, issued in stream order.
+ * Calls that may run concurrently need separate workspaces.
  *
  * This header replaces the reference's torch-typed entry point
  *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)

@@ -372,10 +372,11 @@ def test_c_abi_direct_call(M):
 
 
 def test_shared_workspace_across_shapes():
-    """One workspace serves calls of different shapes in any order (decode stream-K counters)."""
+    """One workspace serves calls of different shapes in any order (decode stream-K partials)."""
     from w4a16_opt import make_workspace, w4a16_gemm_out, workspace_bytes
     shapes = [(1, 4096, 4096), (16, 14336, 4096), (3, 1024, 4096), (8, 28672, 4096), (1, 256, 2048), (5, 4096, 14336)]
     ws = make_workspace(max(workspace_bytes(M, N, K, K // 128) for M, N, K in shapes))
+    ws.fill_(0xFF)   # NaN bit patterns: a call must write every workspace byte it reads
     for rep in range(2):
         for i, (M, N, K) in enumerate(shapes):
             x, q, s, Wp = make_workload(M, N, K, 128, seed=40 + i)

@@ -45,7 +45,7 @@ cudaError_t read_device_status(int* code, bool reset);
 struct DecodePlan {
     int mt;           // 8-token tiles (1: M <= 8, 2: M <= 16)
     int ctas;         // persistent CTAs (one per SM)
-    int units;        // stream-K work units (64 columns x 256 K each)
+    int units;        // stream-K work units (256 columns x one 64-wide K chunk each)
     int stages;       // TMA ring depth
     size_t smem;      // dynamic shared memory bytes
     size_t workspace; // bytes of workspace the launch needs

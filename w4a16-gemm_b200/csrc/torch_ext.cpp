@@ -34,22 +34,21 @@ void check_tensors(const torch::Tensor& Wp, const torch::Tensor& x, const torch:
     TORCH_CHECK(Wp.device() == x.device() && scales.device() == x.device(), "all tensors must be on one device");
 }
 
-// Workspace for the stream-K decode path: one zero-filled buffer per (device,
-// stream), reused by every call on that stream (calls on one stream never
-// overlap, and each completed call leaves the buffer zeroed again).  While the
-// stream is being captured into a CUDA graph a fresh zero-filled buffer is
-// taken from the graph's pool instead, so the zero-fill is part of the graph.
+// Workspace for the stream-K decode path (scratch, no initialisation needed): one
+// buffer per (device, stream), reused by every call on that stream, since calls
+// on one stream never overlap.  While the stream is being captured into a CUDA
+// graph a fresh buffer is taken from the graph's pool instead.
 torch::Tensor workspace_for(const torch::Tensor& x, uint64_t bytes, cudaStream_t stream) {
     if (bytes == 0) return torch::Tensor();
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     TORCH_CHECK(cudaStreamIsCapturing(stream, &cap) == cudaSuccess, "cudaStreamIsCapturing failed");
     auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(x.device());
-    if (cap != cudaStreamCaptureStatusNone) return torch::zeros({(int64_t)bytes}, opts);
+    if (cap != cudaStreamCaptureStatusNone) return torch::empty({(int64_t)bytes}, opts);
     static std::mutex mu;
     static std::map<std::pair<int, cudaStream_t>, torch::Tensor> cache;
     std::lock_guard<std::mutex> lk(mu);
     auto& ws = cache[{x.get_device(), stream}];
-    if (!ws.defined() || (uint64_t)ws.numel() < bytes) ws = torch::zeros({(int64_t)bytes}, opts);
+    if (!ws.defined() || (uint64_t)ws.numel() < bytes) ws = torch::empty({(int64_t)bytes}, opts);
     return ws;
 }
 
@@ -88,8 +87,8 @@ torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor sca
 }
 
 // Same GEMM into a caller-provided contiguous y: fp16, or fp32 for row-parallel partial sums.
-// `workspace` (optional): a zero-filled CUDA buffer of >= workspace_bytes(...) bytes that the
-// caller keeps for calls issued in stream order; otherwise the binding supplies one.
+// `workspace` (optional): a CUDA buffer of >= workspace_bytes(...) bytes that the caller
+// keeps for calls issued in stream order; otherwise the binding supplies one.
 torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, torch::Tensor y,
                                 int64_t variant, c10::optional<torch::Tensor> workspace) {
     check_tensors(Wp, x, scales);

@@ -49,10 +49,9 @@ def w4a16_gemm_out(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, y: t
                    variant: int = -1, workspace: torch.Tensor | None = None) -> torch.Tensor:
     """Same GEMM into a preallocated contiguous ``y`` (fp16, or fp32 for partial sums).
 
-    ``workspace``: optional CUDA buffer, zero-filled once (see ``make_workspace``) and then
-    reused by calls issued in stream order; every call leaves its counter words at zero.
-    Without it the binding keeps one per (device, stream), or zero-fills a fresh one
-    under graph capture.
+    ``workspace``: optional scratch CUDA buffer (see ``make_workspace``; no initialisation
+    needed) reused by calls issued in stream order.  Without it the binding keeps one
+    per (device, stream), or takes a fresh one from the graph pool under capture.
     """
     return _C.w4a16_gemm_out(Wp, x, scales, y, variant, workspace)
 
@@ -63,7 +62,7 @@ def workspace_bytes(M: int, N: int, K: int, groups: int, variant: int = -1) -> i
 
 
 def make_workspace(nbytes: int, device=None) -> torch.Tensor:
-    """A zero-filled workspace buffer of at least ``nbytes`` bytes."""
+    """A workspace buffer of at least ``nbytes`` bytes (zero-filled, though no call needs that)."""
     return torch.zeros(max(256, int(nbytes)), dtype=torch.uint8, device=device or "cuda")
 
 

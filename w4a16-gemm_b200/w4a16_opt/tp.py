@@ -67,7 +67,7 @@ class ColumnParallelW4A16:
         self.N_local = N // self.world
         self.Wp, self.scales = shard_columns(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
-        self.workspace: Optional[torch.Tensor] = None   # optional zero-filled GEMM workspace
+        self.workspace: Optional[torch.Tensor] = None   # optional GEMM workspace (scratch)
 
     def local(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         y = out if out is not None else torch.empty(x.shape[0], self.N_local, dtype=torch.float16, device=x.device)
@@ -103,7 +103,7 @@ class RowParallelW4A16:
         self.K_local = K // self.world
         self.Wp, self.scales = shard_rows(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
-        self.workspace: Optional[torch.Tensor] = None   # optional zero-filled GEMM workspace
+        self.workspace: Optional[torch.Tensor] = None   # optional GEMM workspace (scratch)
 
     def x_slice(self, x: torch.Tensor) -> torch.Tensor:
         return x[:, self.rank * self.K_local:(self.rank + 1) * self.K_local].contiguous()
