@@ -280,6 +280,14 @@ def run_ours(args):
                 u["layer"].local(u["x"], out=u["y_local"])
                 u["layer"].gather(u["y_local"], out=u["y"])
 
+    # kernels of ours per step: each GEMM is decode_kernel (+ decode_fixup_kernel when a column
+    # group is split across CTAs), as the route query reports
+    launches_per_step = 0
+    for u in units:
+        n_loc = u["N"] // (world if "y_local" in u else 1)
+        k_loc = u["K"] // (world if "x_local" in u else 1)
+        launches_per_step += w4a16_opt.query_route(u["M"], n_loc, k_loc, k_loc // DECODE_G)["launches"]
+
     with ClockSampler(smi_index(local)) as clocks:
         ms = graph_time_ms(step, args.steps, args.warmup, world)
     ms_step = ms / args.steps
@@ -311,11 +319,11 @@ def run_ours(args):
                "api": "w4a16_opt.w4a16_gemm (eager, current stream)"}
 
     peaks, peak_kind = load_peaks()
-    traffic = profile_traffic("decode_traffic")
+    traffic = profile_traffic("decode_sweep_traffic")
     roofline = {"bound": "hbm", "kernel": "w4a16::decode_kernel", "achieved": round(value, 1),
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(value / peaks["hbm_gbs"], 4),
                 "peak_source": f"hbm_gbs ({peak_kind})",
-                "traffic": None if traffic is None else traffic.get("bytes_per_step_scaled"),
+                "traffic": None if traffic is None else traffic.get("decode_kernel_dram_bytes_per_step"),
                 "algorithmic_bytes_per_step": step_bytes}
     if world > 1:
         roofline["note"] = "per-rank time includes the NCCL collectives of the TP split"
@@ -380,7 +388,7 @@ def run_ours(args):
                    "parallelism": "single GPU" if world == 1 else f"tp{world} (col: k/v, gate/up; row: q/o, down)",
                    "timing": "CUDA graph of one step, K replays between CUDA events, max over ranks"},
         "e2e": e2e, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
-        "clocks": clocks.summary(), "gpu_launches": len(units) * args.steps,
+        "clocks": clocks.summary(), "gpu_launches": launches_per_step * args.steps,
     }
     print(json.dumps(out), flush=True)
     return 0

@@ -37,7 +37,7 @@
 extern "C" {
 #endif
 
-#define W4A16_ABI_VERSION 1
+#define W4A16_ABI_VERSION 2
 
 typedef enum w4a16_status {
     W4A16_OK = 0,
@@ -68,12 +68,15 @@ typedef struct w4a16_route {
     int32_t kernel;     /* 0 = decode (M <= 16 weight-streaming GEMV), 1 = prefill (tcgen05) */
     int32_t config;     /* prefill tile config 1..4 (token tile 32/64/128/256); 0 for decode */
     int32_t tile_m;     /* tokens per tile (decode: 8 or 16 padded rows) */
-    int32_t tile_n;     /* output channels per tile (decode 64, prefill 128) */
-    int32_t split_k;    /* decode: stream-K work units (64 columns x 256 K); prefill: 1 */
+    int32_t tile_n;     /* output channels per tile (decode 256, prefill 128) */
+    int32_t split_k;    /* decode: stream-K work units (256 columns x one 64-wide K chunk); prefill: 1 */
     int32_t grid;       /* CTAs launched */
     int32_t stages;     /* pipeline depth */
     int32_t smem_bytes; /* dynamic shared memory per CTA */
     uint64_t workspace_bytes; /* workspace the call needs (see w4a16_workspace_bytes) */
+    int32_t launches;   /* kernels one call launches (decode: 2 when a column group is split
+                           across CTAs -- the combine kernel runs behind the main one) */
+    int32_t reserved;
 } w4a16_route;
 
 /* Version of this ABI (W4A16_ABI_VERSION). */

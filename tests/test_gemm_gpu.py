@@ -334,11 +334,13 @@ def test_query_route():
     from w4a16_opt import query_route
     r = query_route(1, 4096, 4096, 32)
     assert r["kernel"] == "decode" and r["grid"] == torch.cuda.get_device_properties(0).multi_processor_count
-    assert r["workspace_bytes"] > 0
+    assert r["workspace_bytes"] > 0 and r["launches"] == 2   # 16 groups over 148 CTAs: split
+    sms = torch.cuda.get_device_properties(0).multi_processor_count
+    assert query_route(1, 256 * sms, 64, 1)["launches"] == 1   # one whole 256-column group per CTA
     r = query_route(3, 4112, 4160, 65)
     assert r["kernel"] == "decode"
     r = query_route(2048, 14336, 4096, 32)
-    assert r["kernel"] == "prefill" and r["grid"] <= 148
+    assert r["kernel"] == "prefill" and r["grid"] <= 148 and r["launches"] == 1
     for v in PREFILL_VARIANTS:
         assert query_route(5, 4096, 4096, 32, v)["config"] == v
     assert query_route(5, 4096, 4096, 32, 0)["kernel"] == "decode"

@@ -152,6 +152,7 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
         out->grid = r.dp.ctas;
         out->stages = r.dp.stages;
         out->smem_bytes = (int32_t)r.dp.smem;
+        out->launches = r.dp.launches;
     } else {
         out->kernel = 1;
         out->config = r.pp.config;
@@ -161,6 +162,7 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
         out->grid = r.pp.grid;
         out->stages = r.pp.stages;
         out->smem_bytes = (int32_t)r.pp.smem;
+        out->launches = 1;
     }
     return ok();
 }

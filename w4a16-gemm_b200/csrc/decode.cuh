@@ -189,7 +189,7 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
         st.start(c0, c1, KC);
         for (int t = 0; st.more(); ++t) {
             const int nk = st.nk(KC), s = t % XT;
-            if (t >= XT && !__all_sync(0xffffffffu, mbar_wait(xempty(s), ((t / XT) - 1) & 1, kDevTimeoutActivations)))
+            if (t >= XT && !__all_sync(0xffffffffu, mbar_wait_sleep(xempty(s), ((t / XT) - 1) & 1, kDevTimeoutActivations)))
                 break;
             const uint32_t stage = xbuf + s * C::STAGE_BYTES;
             // rows < M: this step's nk chunks; pieces beyond them are zero-filled
@@ -254,20 +254,20 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
     for (; st.more(); ++t) {
         const int nk = st.nk(KC), s = t % XT, r = t % R;
         const bool active = st.g * kDcWarps + warp < NB;
-        ok = __all_sync(0xffffffffu, mbar_wait(xfull(s), (t / XT) & 1, kDevTimeoutActivations));
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait(wfull(r), (t / R) & 1, kDevTimeoutWeights));
+        ok = __all_sync(0xffffffffu, mbar_wait_sleep(xfull(s), (t / XT) & 1, kDevTimeoutActivations));
+        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep(wfull(r), (t / R) & 1, kDevTimeoutWeights));
         if (!ok) break;
         if (active) {
             const uint32_t stage = xbuf + s * C::STAGE_BYTES;
-            const uint8_t* sp = gbase + (stage - base) + s_lane;
+            const uint32_t sp = stage + s_lane;
             // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are 0 too)
             uint32_t s_lo[kDcStep], s_hi[kDcStep];
             const int r0 = (st.kc * 64) / G;
 #pragma unroll
             for (int j = 0; j < kDcStep; ++j) {
                 const int row = ((st.kc + (j < nk ? j : 0)) * 64) / G - r0;
-                const unsigned short lo = *reinterpret_cast<const unsigned short*>(sp + row * C::SROW);
-                const unsigned short hi = *reinterpret_cast<const unsigned short*>(sp + row * C::SROW + 16);
+                const uint16_t lo = lds_u16(sp + row * C::SROW);
+                const uint16_t hi = lds_u16(sp + row * C::SROW + 16);
                 s_lo[j] = j < nk ? bcast_half(lo) : 0u;
                 s_hi[j] = j < nk ? bcast_half(hi) : 0u;
             }
@@ -395,6 +395,7 @@ DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
     p.stages = DcCfg<8>::R;
     p.smem = p.mt == 1 ? DcCfg<8>::SMEM : DcCfg<16>::SMEM;
     p.workspace = dc_workspace_bytes(part);
+    p.launches = dc_has_split(part) ? 2 : 1;
     p.valid = part.valid;
     return p;
 }

@@ -16,7 +16,7 @@ struct GemmArgs {
     bool out_f32;         // fp32 output (tensor-parallel partials) instead of fp16
     cudaStream_t stream;
     bool pdl;             // launch with programmatic dependent launch enabled
-    void* workspace;      // zero-initialised before first use; left zeroed by every call
+    void* workspace;      // decode scratch (split-group partials); no initial contents needed
     size_t workspace_bytes;
 };
 
@@ -49,6 +49,7 @@ struct DecodePlan {
     int stages;       // TMA ring depth
     size_t smem;      // dynamic shared memory bytes
     size_t workspace; // bytes of workspace the launch needs
+    int launches;     // kernels launched: 1, or 2 when a group is split (combine kernel)
     bool valid;
 };
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);

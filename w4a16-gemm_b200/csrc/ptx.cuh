@@ -15,6 +15,7 @@ namespace w4a16 {
 // Wall-clock bound for any single wait inside a kernel.  Far above any
 // legitimate wait (a whole kernel runs in microseconds to milliseconds).
 constexpr uint64_t kWaitLimitNs = 2000000000ull;   // 2 s
+constexpr uint32_t kWaitHintNs = 10000;            // suspend-time hint of one sleeping poll
 
 // Error codes written to the device status word.
 enum DeviceError : int {
@@ -84,6 +85,32 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t par
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
+}
+
+// try_wait with a suspend-time hint: a waiting thread sleeps until the phase
+// completes (or the hint elapses) instead of re-issuing, leaving issue slots to
+// the warps that compute.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok) : "r"(bar), "r"(parity), "n"(kWaitHintNs) : "memory");
+    return ok != 0;
+}
+
+// Bounded wait that sleeps between polls (see mbar_try_wait_sleep).
+__device__ __forceinline__ bool mbar_wait_sleep(uint32_t bar, uint32_t parity, int code) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = globaltimer_ns();
+    while (true) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if (globaltimer_ns() - t0 > kWaitLimitNs) {
+            record_device_error(code);
+            return false;
+        }
+    }
 }
 
 // Bounded wait for phase `parity` of a CTA-local mbarrier.  Returns false (and
@@ -230,6 +257,12 @@ __device__ __forceinline__ void pdl_launch_dependents() {
 __device__ __forceinline__ void ldmatrix_x4(uint32_t (&r)[4], uint32_t addr) {
     asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]) : "r"(addr));
+}
+
+__device__ __forceinline__ uint16_t lds_u16(uint32_t addr) {
+    uint16_t v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(addr));
+    return v;
 }
 
 __device__ __forceinline__ uint4 lds128(uint32_t addr) {

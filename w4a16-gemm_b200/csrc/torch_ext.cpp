@@ -137,6 +137,7 @@ pybind11::dict query_route_py(int64_t M, int64_t N, int64_t K, int64_t groups, i
     d["stages"] = r.stages;
     d["smem_bytes"] = r.smem_bytes;
     d["workspace_bytes"] = r.workspace_bytes;
+    d["launches"] = r.launches;
     return d;
 }
 

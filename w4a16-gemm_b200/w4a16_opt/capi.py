@@ -28,7 +28,7 @@ STATUS_NAMES = {
 class Route(ctypes.Structure):
     _fields_ = [(name, ctypes.c_int32) for name in
                 ("kernel", "config", "tile_m", "tile_n", "split_k", "grid", "stages", "smem_bytes")] + \
-               [("workspace_bytes", ctypes.c_uint64)]
+               [("workspace_bytes", ctypes.c_uint64), ("launches", ctypes.c_int32), ("reserved", ctypes.c_int32)]
 
 
 _i64, _i32, _u64, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p
