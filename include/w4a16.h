@@ -39,6 +39,10 @@ extern "C" {
 
 #define W4A16_ABI_VERSION 2
 
+/* Size of the scratch array built into the library for w4a16_gemm_noalloc
+ * (6 MiB per device: the decode path's partials on a GPU of up to 192 SMs). */
+#define W4A16_NOALLOC_SCRATCH_BYTES (6u << 20)
+
 typedef enum w4a16_status {
     W4A16_OK = 0,
     W4A16_ERR_NULL_POINTER = 1,      /* a required pointer is NULL */
@@ -103,6 +107,22 @@ w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, vo
                         int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
                         int32_t variant, int32_t out_dtype, void* workspace, uint64_t workspace_bytes,
                         void* stream);
+
+/* Same GEMM as w4a16_gemm for callers that cannot allocate device memory
+ * (fixed device-memory budgets, bindings without a device allocator).  No
+ * counterpart in the reference, whose entry point allocates y itself.  The
+ * scratch the decode path needs comes from an array of
+ * W4A16_NOALLOC_SCRATCH_BYTES built into the library instead of a caller
+ * workspace; y stays caller-allocated.  Nothing in it needs to start at zero.
+ * Limits: a call whose scratch need exceeds the array fails with
+ * W4A16_ERR_WORKSPACE; every call on a device uses the same array, so calls
+ * that overlap in time (other streams, other host threads) race -- serialise
+ * them.  The first call on each device does a one-time set-up (it looks up the
+ * array's device address with that device current), so make it before any
+ * stream capture. */
+w4a16_status w4a16_gemm_noalloc(const int32_t* Wp, const void* x, const void* scales, void* y,
+                                int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
+                                int32_t variant, int32_t out_dtype, void* stream);
 
 /* The launch w4a16_gemm would make for this call (kernel choice, tiles, grid).
  * Mirrors the reference's routing (kernel.cu:242-249) and prefill config

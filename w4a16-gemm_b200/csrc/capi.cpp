@@ -134,6 +134,28 @@ w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, vo
     return ok();
 }
 
+// The GEMM with the library's built-in scratch in place of a caller workspace: the
+// same validation, routing and kernels as w4a16_gemm, which it calls.
+w4a16_status w4a16_gemm_noalloc(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
+                                int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
+                                void* stream) {
+    w4a16_status s = w4a16_validate(Wp, x, scales, M, N, K, groups, wp_words, variant);
+    if (s != W4A16_OK) return s;
+    uint64_t need = 0;
+    if ((s = w4a16_workspace_bytes(M, N, K, groups, variant, &need)) != W4A16_OK) return s;
+    if (need == 0)
+        return w4a16_gemm(Wp, x, scales, y, M, N, K, groups, wp_words, variant, out_dtype, nullptr, 0, stream);
+    void* scratch = nullptr;
+    size_t cap = 0;
+    const cudaError_t err = w4a16::noalloc_scratch(&scratch, &cap);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    if (need > cap)
+        return fail(W4A16_ERR_WORKSPACE, "this call needs " + std::to_string(need) +
+                                             " bytes of scratch; the built-in scratch holds " + std::to_string(cap) +
+                                             " (use w4a16_gemm with a caller workspace)");
+    return w4a16_gemm(Wp, x, scales, y, M, N, K, groups, wp_words, variant, out_dtype, scratch, cap, stream);
+}
+
 w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, int32_t variant, w4a16_route* out) {
     w4a16_status s = w4a16_validate(nullptr, nullptr, nullptr, M, N, K, groups, N * K / 8, variant);
     if (s != W4A16_OK) return s;

@@ -4,6 +4,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include "../../include/w4a16.h"
+
 namespace w4a16 {
 
 // One validated GEMM call: y[M, N] = x[M, K] @ W^T, W from packed nibbles + fp16 scales.
@@ -40,6 +42,13 @@ cudaError_t ensure_nonportable_cluster(const void* func);
 // Read (and optionally clear) the device status word that bounded waits set on
 // timeout.  Synchronises with the device.
 cudaError_t read_device_status(int* code, bool reset);
+
+// Built-in scratch of w4a16_gemm_noalloc: a device array of kNoAllocScratchBytes
+// compiled into the library.  Returns its address on the current device (looked
+// up once per device).
+constexpr size_t kNoAllocScratchBytes = W4A16_NOALLOC_SCRATCH_BYTES;
+constexpr int kMaxDevices = 64;
+cudaError_t noalloc_scratch(void** ptr, size_t* bytes);
 
 // ---------------------------------------------------------------- decode (M <= 16)
 struct DecodePlan {

@@ -123,4 +123,34 @@ cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx
     return cudaSuccess;
 }
 
+// ---------------------------------------------------------------- built-in scratch (w4a16_gemm_noalloc)
+// Scratch for callers that are not allowed to allocate device memory themselves:
+// e.g. a host integration whose device memory budget is fixed at start-up, or a
+// foreign-language binding with no device allocator to hand a workspace from.
+// The decode path's split-group partials then live in this array, which the
+// module loader reserves on every device alongside the kernels; nothing is
+// allocated per call.  The kernels write every byte of it they read, so its
+// contents never need to start at zero.  All calls on one device share it.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
+
+cudaError_t noalloc_scratch(void** ptr, size_t* bytes) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    static std::mutex mu;
+    static void* addr[kMaxDevices] = {};
+    std::lock_guard<std::mutex> lk(mu);
+    if (!addr[dev]) {
+        // one-time set-up for this device (with it current): the array's device address
+        void* p = nullptr;
+        err = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+        if (err != cudaSuccess) return err;
+        addr[dev] = p;
+    }
+    *ptr = addr[dev];
+    *bytes = kNoAllocScratchBytes;
+    return cudaSuccess;
+}
+
 }  // namespace w4a16

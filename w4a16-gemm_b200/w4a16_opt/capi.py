@@ -39,6 +39,7 @@ EXPORTS = {
     "w4a16_validate": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32]),
     "w4a16_workspace_bytes": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)]),
     "w4a16_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp, _u64, _vp]),
+    "w4a16_gemm_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "w4a16_query_route": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(Route)]),
     "w4a16_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
     "w4a16_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
