@@ -80,12 +80,13 @@ class ColumnParallelW4A16:
 
     def gather(self, y_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         M = y_local.shape[0]
-        buf = torch.empty(self.world, M, self.N_local, dtype=y_local.dtype, device=y_local.device)
+        # ranks' blocks concatenated along dim 0 ([world * M, N/P]: the layout every backend takes)
+        buf = torch.empty(self.world * M, self.N_local, dtype=y_local.dtype, device=y_local.device)
         dist.all_gather_into_tensor(buf, y_local.contiguous(), group=self.group)
         if M == 1:
             return buf.view(1, self.N)
         y = out if out is not None else torch.empty(M, self.N, dtype=y_local.dtype, device=y_local.device)
-        y.view(M, self.world, self.N_local).copy_(buf.permute(1, 0, 2))
+        y.view(M, self.world, self.N_local).copy_(buf.view(self.world, M, self.N_local).permute(1, 0, 2))
         return y
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
