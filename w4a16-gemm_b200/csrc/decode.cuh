@@ -53,18 +53,17 @@ constexpr int kDcMaxCTAs = 1024;
 
 template <int MP>
 struct DcCfg {
-    static constexpr int R = 4;                                   // per-warp packed-word ring depth (steps)
-    static constexpr int XT = 4;                                  // activation / scale stages
-    static constexpr int WSTEP = kDcStep * 512;                   // one warp's packed words of a step (2 KB)
-    static constexpr int RING_BYTES = kDcWarps * R * WSTEP;
-    static constexpr int XROW = kDcStep * 128 + 16;               // one token row of a step (+16 B: conflict-free)
-    static constexpr int SROWS = 4;                               // scale rows a step can touch (G = 64)
-    static constexpr int SROW = kDcCols * 2;                      // one scale row of a group
-    static constexpr int STAGE_BYTES = MP * XROW + SROWS * SROW;
-    static constexpr int XBUF_BYTES = XT * STAGE_BYTES;
-    static constexpr int BAR_BYTES = (kDcWarps * R + 2 * XT) * 8;
-    static constexpr int SMEM = 128 + RING_BYTES + XBUF_BYTES + BAR_BYTES;
-    static_assert(STAGE_BYTES % 16 == 0, "stage alignment");
+    static constexpr int ST = 4;                                  // stages: steps in flight
+    static constexpr int W_CHUNK = kDcWarps * 512;                // packed words of one chunk of a group (8 KB)
+    static constexpr int W_BYTES = kDcStep * W_CHUNK;             // [chunk][n16 block][32 lanes x 16 B]
+    static constexpr int X_CHUNK = MP * 128;                      // one chunk's token rows (128-byte swizzle)
+    static constexpr int X_BYTES = kDcStep * X_CHUNK;
+    static constexpr int SROW = kDcCols * 2;                      // one chunk's scales of the group (512 B)
+    static constexpr int S_BYTES = kDcStep * SROW;
+    static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + S_BYTES;
+    static constexpr int BAR_BYTES = 2 * ST * 8;
+    static constexpr int SMEM = 1024 + ST * STAGE_BYTES + BAR_BYTES;
+    static_assert(STAGE_BYTES % 1024 == 0 && X_CHUNK % 1024 == 0, "stage alignment (128-byte swizzle atoms)");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -121,11 +120,6 @@ __host__ __device__ inline size_t dc_workspace_bytes(const DcPartition& p) {
     return (size_t)2 * p.ctas * kDcSlotFloats * 4;
 }
 
-// 16-byte cp.async that reads src_bytes (0 or 16) and zero-fills the rest.
-__device__ __forceinline__ void cp_async16_zfill(uint32_t dst, const void* src, uint32_t src_bytes) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"(dst), "l"(src), "r"(src_bytes) : "memory");
-}
-
 // Walks a CTA's chunk range [pos, end) in steps of <= kDcStep chunks that never
 // cross a group boundary.
 struct DcSteps {
@@ -144,99 +138,103 @@ struct DcSteps {
 
 template <int G, int MP, bool OUT_F32>
 __global__ void __launch_bounds__(kDcThreads, 1)
-decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
-              const __half* __restrict__ scales, void* __restrict__ yv, int M, int N, int K,
+decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
+              const __grid_constant__ CUtensorMap ts, void* __restrict__ yv, int M, int N, int box_blocks,
               DcPartition part, float* __restrict__ partials)
 {
     using C = DcCfg<MP>;
-    constexpr int R = C::R;
-    constexpr int XT = C::XT;
+    constexpr int ST = C::ST;
     constexpr int MT = MP / 8;
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
-    const uint32_t base = (raw + 127u) & ~127u;
+    const uint32_t base = (raw + 1023u) & ~1023u;
     uint8_t* const gbase = smem_raw + (base - raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-    const uint32_t xbuf = base + C::RING_BYTES;
-    const uint32_t bars = xbuf + C::XBUF_BYTES;
-    auto wfull = [&](int r) { return bars + (uint32_t)(warp * R + r) * 8; };
-    auto xfull = [&](int s) { return bars + (uint32_t)(kDcWarps * R + s) * 8; };
-    auto xempty = [&](int s) { return bars + (uint32_t)(kDcWarps * R + XT + s) * 8; };
+    const uint32_t bars = base + ST * C::STAGE_BYTES;
+    auto stage = [&](int s) { return base + (uint32_t)s * C::STAGE_BYTES; };
+    auto full = [&](int s) { return bars + (uint32_t)s * 8; };
+    auto empty = [&](int s) { return bars + (uint32_t)(ST + s) * 8; };
 
     const int c = blockIdx.x;
     const int c0 = part.c0(c), c1 = part.c0(c + 1);
     const int KC = part.kc, NB = N >> 4;
 
     if (threadIdx.x == 0) {
-        for (int i = 0; i < kDcWarps * R; ++i) mbar_init(bars + 8 * i, 1);
-        for (int s = 0; s < XT; ++s) {
-            mbar_init(xfull(s), 32);          // the producer's 32 lanes (cp.async arrivals)
-            mbar_init(xempty(s), kDcWarps);   // one arrival per consumer warp
+        for (int s = 0; s < ST; ++s) {
+            mbar_init(full(s), 1);           // the producer's arrive.expect_tx + all tensor-copy bytes
+            mbar_init(empty(s), kDcWarps);   // one arrival per consumer warp
         }
     }
     fence_mbar_init();
-    // Token rows M..MP-1 of every stage stay zero (only rows < M are ever copied).
-    for (int i = threadIdx.x; i < C::XBUF_BYTES / 16; i += kDcThreads)
-        reinterpret_cast<uint4*>(gbase + C::RING_BYTES)[i] = make_uint4(0, 0, 0, 0);
+    // Token rows start zeroed: chunks a step does not load keep finite contents (zeros or
+    // earlier activations), which their zero scales cancel.
+    for (int s = 0; s < ST; ++s)
+        for (int i = threadIdx.x; i < C::X_BYTES / 16; i += kDcThreads)
+            reinterpret_cast<uint4*>(gbase + s * C::STAGE_BYTES + C::W_BYTES)[i] = make_uint4(0, 0, 0, 0);
     __syncthreads();
 
     if (warp == kDcWarps) {
-        // ------------------------------------------------ producer: activations + scales
-        pdl_wait();   // x may still be written by the previous kernel
-        pdl_launch_dependents();
+        // ------------------------------------------------ producer (one lane): all of a step by tensor copies
+        // Per chunk j of a step: the packed words of up to 16 n16 blocks (box 16 x 512 B; blocks
+        // beyond N zero-filled) into [chunk][block][512 B]; the token rows (box 64 x MP fp16,
+        // rows >= M zero-filled, 128-byte swizzle); the group's scales of the chunk (box 256 x 1).
+        if (lane != 0) return;
+        const uint32_t w_bytes = (uint32_t)box_blocks * 512, s_bytes = (uint32_t)(box_blocks * 16 * 2);
+        auto issue_weights = [&](int s, const DcSteps& w, int nk) {   // packed words + scales
+            mbar_expect_tx(full(s), (uint32_t)nk * (w_bytes + s_bytes));
+            for (int j = 0; j < nk; ++j) {
+                tma_load_3d(stage(s) + j * C::W_CHUNK, &tw, 0, w.kc + j, w.g * kDcWarps, full(s));
+                tma_load_2d(stage(s) + C::W_BYTES + C::X_BYTES + j * C::SROW, &ts, w.g * kDcCols,
+                            ((w.kc + j) * 64) / G, full(s));
+            }
+        };
         DcSteps st;
         st.start(c0, c1, KC);
-        for (int t = 0; st.more(); ++t) {
-            const int nk = st.nk(KC), s = t % XT;
-            if (t >= XT && !__all_sync(0xffffffffu, mbar_wait_sleep(xempty(s), ((t / XT) - 1) & 1, kDevTimeoutActivations)))
-                break;
-            const uint32_t stage = xbuf + s * C::STAGE_BYTES;
-            // rows < M: this step's nk chunks; pieces beyond them are zero-filled
-            const __half* xs = x + (size_t)st.kc * 64 + lane * 8;
-            const uint32_t xsrc = lane < nk * 8 ? 16u : 0u;
-            for (int m = 0; m < M; ++m)
-                cp_async16_zfill(stage + m * C::XROW + lane * 16, xsrc ? xs + (size_t)m * K : x, xsrc);
-            // the group's scale rows this step touches (columns beyond N are never read)
-            const int r0 = (st.kc * 64) / G, r1 = ((st.kc + nk - 1) * 64) / G;
-            const int col = st.g * kDcCols + lane * 8;
-            if (col < N)
-                for (int r = r0; r <= r1; ++r)
-                    cp_async16(stage + MP * C::XROW + (r - r0) * C::SROW + lane * 16, scales + (size_t)r * N + col);
-            cp_async_arrive_noinc(xfull(s));
+        prefetch_tmap(&tw);
+        prefetch_tmap(&tx);
+        prefetch_tmap(&ts);
+        {
+            DcSteps w = st;                  // weights and scales never depend on the previous kernel
+            for (int t = 0; t < ST && w.more(); ++t) {
+                const int nk = w.nk(KC);
+                issue_weights(t, w, nk);
+                w.advance(nk, KC);
+            }
+        }
+        pdl_wait();   // x may still be written by the previous kernel
+        pdl_launch_dependents();
+        int t = 0;
+        for (; st.more(); ++t) {
+            const int nk = st.nk(KC), s = t % ST;
+            if (t >= ST) {
+                if (!mbar_wait_sleep(empty(s), ((t / ST) - 1) & 1, kDevTimeoutActivations)) break;
+                issue_weights(s, st, nk);
+            }
+            mbar_arrive_expect_tx(full(s), (uint32_t)(nk * C::X_CHUNK));
+            for (int j = 0; j < nk; ++j)
+                tma_load_2d(stage(s) + C::W_BYTES + j * C::X_CHUNK, &tx, (st.kc + j) * 64, 0, full(s));
             st.advance(nk, KC);
         }
-        asm volatile("cp.async.wait_all;" ::: "memory");
+        // Tensor copies still in flight must land before the CTA may exit: normally the last ST
+        // phases have completed already; after a consumer timeout they may not have.  (A break
+        // happens only at t >= ST, after every step issued ahead of the loop got its arrival.)
+        for (int j = t - 1; j >= 0 && j >= t - ST; --j) mbar_wait(full(j % ST), (j / ST) & 1, kDevTimeoutDrain);
         return;
     }
 
     // ---------------------------------------------------- consumer warp: n16 block `warp` of each group
     const int g8 = lane >> 2, t4 = lane & 3;
-    const uint32_t ring = base + warp * R * C::WSTEP;
-    DcSteps is;                       // lane 0: the step whose packed words are issued next
-    is.start(c0, c1, KC);
-    int t_issue = 0;
-    auto issue_w = [&]() {            // lane 0 only
-        if (!is.more()) return;
-        const int nk = is.nk(KC), r = t_issue % R;
-        const int nb = is.g * kDcWarps + warp;
-        if (nb < NB) {
-            mbar_arrive_expect_tx(wfull(r), (uint32_t)(nk * 512));
-            bulk_g2s(ring + r * C::WSTEP, wp + ((size_t)nb * KC + is.kc) * 512, (uint32_t)(nk * 512), wfull(r));
-        } else {
-            mbar_arrive(wfull(r));    // block beyond N: nothing to load, keep the phases in step
-        }
-        is.advance(nk, KC);
-        ++t_issue;
-    };
-    if (lane == 0)
-        for (int j = 0; j < R; ++j) issue_w();
     pdl_wait();   // the workspace and y may still be in use by the previous kernel
     pdl_launch_dependents();
 
-    const uint32_t w_lane = (uint32_t)(lane * 16);
-    const uint32_t x_lane = (uint32_t)((lane & 7) * C::XROW + (lane >> 3) * 16);
-    const uint32_t s_lane = (uint32_t)(MP * C::XROW + warp * 32 + g8 * 2);
+    const uint32_t w_lane = (uint32_t)(warp * 512 + lane * 16);
+    // ldmatrix row addresses in a 128-byte-swizzled chunk of token rows: row r's 16-byte unit u
+    // sits at unit u ^ (r % 8); lanes 8i..8i+7 address rows 0..7 of 8x8 matrix i (k units i, i+4)
+    const uint32_t xr = (uint32_t)(lane & 7), xu = (uint32_t)(lane >> 3);
+    const uint32_t x_lane0 = C::W_BYTES + xr * 128 + ((xu ^ xr) << 4);
+    const uint32_t x_lane1 = C::W_BYTES + xr * 128 + (((xu + 4) ^ xr) << 4);
+    const uint32_t s_lane = (uint32_t)(C::W_BYTES + C::X_BYTES + warp * 32 + g8 * 2);
 
     float acc[kDcStep][MT][4];
 #pragma unroll
@@ -246,33 +244,25 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[j][mt][i] = 0.f;
 
-    bool ok = true;
     DcSteps st;
     st.start(c0, c1, KC);
     int gkc0 = st.kc;                 // first chunk of the current group inside this CTA
-    int t = 0;
-    for (; st.more(); ++t) {
-        const int nk = st.nk(KC), s = t % XT, r = t % R;
+    for (int t = 0; st.more(); ++t) {
+        const int nk = st.nk(KC), s = t % ST;
         const bool active = st.g * kDcWarps + warp < NB;
-        ok = __all_sync(0xffffffffu, mbar_wait_sleep(xfull(s), (t / XT) & 1, kDevTimeoutActivations));
-        if (ok) ok = __all_sync(0xffffffffu, mbar_wait_sleep(wfull(r), (t / R) & 1, kDevTimeoutWeights));
-        if (!ok) break;
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(full(s), (t / ST) & 1, kDevTimeoutWeights))) break;
         if (active) {
-            const uint32_t stage = xbuf + s * C::STAGE_BYTES;
-            const uint32_t sp = stage + s_lane;
+            const uint32_t sb = stage(s);
             // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are 0 too)
             uint32_t s_lo[kDcStep], s_hi[kDcStep];
-            const int r0 = (st.kc * 64) / G;
 #pragma unroll
             for (int j = 0; j < kDcStep; ++j) {
-                const int row = ((st.kc + (j < nk ? j : 0)) * 64) / G - r0;
-                const uint16_t lo = lds_u16(sp + row * C::SROW);
-                const uint16_t hi = lds_u16(sp + row * C::SROW + 16);
+                const uint16_t lo = lds_u16(sb + s_lane + j * C::SROW);
+                const uint16_t hi = lds_u16(sb + s_lane + j * C::SROW + 16);
                 s_lo[j] = j < nk ? bcast_half(lo) : 0u;
                 s_hi[j] = j < nk ? bcast_half(hi) : 0u;
             }
-            const uint32_t wb = ring + r * C::WSTEP + w_lane;
-            const uint32_t xb = stage + x_lane;
+            const uint32_t wb = sb + w_lane;
             constexpr int JB = MT == 1 ? 4 : 2;
 #pragma unroll
             for (int jb = 0; jb < kDcStep; jb += JB) {
@@ -280,12 +270,12 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
                 uint32_t b[JB][MT][8];
 #pragma unroll
                 for (int jj = 0; jj < JB; ++jj) {
-                    wv[jj] = lds128(wb + (jb + jj) * 512);
+                    wv[jj] = lds128(wb + (jb + jj) * C::W_CHUNK);
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
-                        const uint32_t xa = xb + mt * 8 * C::XROW + (jb + jj) * 128;
-                        ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][0]), xa);
-                        ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][4]), xa + 64);
+                        const uint32_t xa = sb + (jb + jj) * C::X_CHUNK + mt * 1024;
+                        ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][0]), xa + x_lane0);
+                        ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][4]), xa + x_lane1);
                     }
                 }
                 // No per-chunk guard: the unconditional body lets the 4 accumulator chains interleave.
@@ -302,12 +292,9 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
                     }
             }
         }
-        // release the stage, refill this ring slot R steps ahead
+        // release the stage to the producer
         __syncwarp();
-        if (lane == 0) {
-            mbar_arrive(xempty(s));
-            issue_w();
-        }
+        if (lane == 0) mbar_arrive(empty(s));
         const int g = st.g;
         const bool whole_end = st.kc + nk == KC && gkc0 == 0;
         if (st.advance(nk, KC)) {
@@ -338,13 +325,6 @@ decode_kernel(const uint8_t* __restrict__ wp, const __half* __restrict__ x,
                     }
             }
             gkc0 = 0;
-        }
-    }
-    if (!ok) {
-        // Error path: let this warp's copies still in flight land before the CTA may exit.
-        for (int j = t; j < t + R; ++j) {
-            if (!__shfl_sync(0xffffffffu, j < t_issue ? 1 : 0, 0)) break;
-            mbar_wait(wfull(j % R), (j / R) & 1, kDevTimeoutDrain);
         }
     }
 }
@@ -392,7 +372,7 @@ DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
     p.mt = M <= 8 ? 1 : 2;
     p.ctas = part.ctas;
     p.units = part.total;
-    p.stages = DcCfg<8>::R;
+    p.stages = DcCfg<8>::ST;
     p.smem = p.mt == 1 ? DcCfg<8>::SMEM : DcCfg<16>::SMEM;
     p.workspace = dc_workspace_bytes(part);
     p.launches = dc_has_split(part) ? 2 : 1;
@@ -404,6 +384,12 @@ size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev) {
     return dc_workspace_bytes(dc_partition(N, K, dev.num_sms));
 }
 
+// Tensor maps of the decode kernel (kernels.cu): packed words viewed as [NB][KC][128] int32,
+// box {128, 1, box_blocks} (one 64-wide chunk of up to 16 n16 blocks); x [M, K] fp16, box
+// {64, MP} with 128-byte swizzle; scales [K/G, N] fp16, box {16 * box_blocks, 1}.
+cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int mp, CUtensorMap* tw, CUtensorMap* tx,
+                                    CUtensorMap* ts);
+
 template <int G, int MP, bool F32>
 static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     auto kern = decode_kernel<G, MP, F32>;
@@ -413,6 +399,9 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     if ((err = device_info(&dev)) != cudaSuccess) return err;
     const DcPartition part = dc_partition(a.N, a.K, dev.num_sms);
     float* partials = static_cast<float*>(a.workspace);
+    const int box_blocks = std::min(kDcWarps, a.N / 16);
+    CUtensorMap tw, tx, ts;
+    if ((err = make_decode_tensor_maps(a, box_blocks, MP, &tw, &tx, &ts)) != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(part.ctas, 1, 1);
     cfg.blockDim = dim3(kDcThreads, 1, 1);   // 16 consumer warps + 1 producer warp
@@ -423,8 +412,7 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    err = cudaLaunchKernelEx(&cfg, kern, static_cast<const uint8_t*>(a.wp), static_cast<const __half*>(a.x),
-                             static_cast<const __half*>(a.scales), a.y, a.M, a.N, a.K, part, partials);
+    err = cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, part, partials);
     if (err != cudaSuccess || !dc_has_split(part)) return err;
     // combine split groups; always launched programmatically dependent on decode_kernel
     cudaLaunchConfig_t fc = {};

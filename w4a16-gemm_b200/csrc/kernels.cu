@@ -123,6 +123,41 @@ cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx
     return cudaSuccess;
 }
 
+cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int mp, CUtensorMap* tw, CUtensorMap* tx,
+                                    CUtensorMap* ts) {
+    auto encode = tensor_map_encoder();
+    if (!encode) return cudaErrorNotSupported;
+    const cuuint32_t one[3] = {1, 1, 1};
+    {   // packed words [NB][KC][128] int32, box {128, 1, box_blocks}
+        const cuuint64_t dims[3] = {128, (cuuint64_t)(a.K / 64), (cuuint64_t)(a.N / 16)};
+        const cuuint64_t strides[2] = {512, (cuuint64_t)(a.K / 64) * 512};
+        const cuuint32_t box[3] = {128, 1, (cuuint32_t)box_blocks};
+        if (encode(tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<void*>(a.wp), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {   // x [M, K] fp16, box {64, mp} (rows >= M read as zeros), 128-byte swizzle
+        const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
+        const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
+        const cuuint32_t box[2] = {64, (cuuint32_t)mp};
+        if (encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    {   // scales [K/G, N] fp16, box {16 * box_blocks, 1}
+        const cuuint64_t dims[2] = {(cuuint64_t)a.N, (cuuint64_t)(a.K / a.G)};
+        const cuuint64_t strides[1] = {(cuuint64_t)a.N * 2};
+        const cuuint32_t box[2] = {(cuuint32_t)(16 * box_blocks), 1};
+        if (encode(ts, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.scales), dims, strides, box, one,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cudaErrorInvalidValue;
+    }
+    return cudaSuccess;
+}
+
 // ---------------------------------------------------------------- built-in scratch (w4a16_gemm_noalloc)
 // Scratch for callers that are not allowed to allocate device memory themselves:
 // e.g. a host integration whose device memory budget is fixed at start-up, or a
