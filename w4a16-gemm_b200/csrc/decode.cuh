@@ -44,9 +44,14 @@
 
 namespace w4a16 {
 
-constexpr int kDcWarps = 16;                              // consumer warps; warp w owns n16 block w of a group
-constexpr int kDcThreads = (kDcWarps + 1) * 32;           // + the activation / scale producer warp
-constexpr int kDcCols = kDcWarps * 16;                    // output columns per group
+constexpr int kDcBlocks = 16;                             // n16 blocks per group
+#ifndef W4A16_DC_BPW
+#define W4A16_DC_BPW 2
+#endif
+constexpr int kDcBPW = W4A16_DC_BPW;                      // n16 blocks per consumer warp
+constexpr int kDcWarps = kDcBlocks / kDcBPW;              // consumer warps; warp w owns blocks w*BPW.. of a group
+constexpr int kDcThreads = (kDcWarps + 1) * 32;           // + the producer warp
+constexpr int kDcCols = kDcBlocks * 16;                   // output columns per group
 constexpr int kDcStep = 4;                                // 64-wide K chunks per step
 constexpr int kDcSlotFloats = 16 * kDcCols;               // one partial: 16 tokens x 256 columns
 constexpr int kDcMaxCTAs = 1024;
@@ -54,7 +59,7 @@ constexpr int kDcMaxCTAs = 1024;
 template <int MP>
 struct DcCfg {
     static constexpr int ST = 4;                                  // stages: steps in flight
-    static constexpr int W_CHUNK = kDcWarps * 512;                // packed words of one chunk of a group (8 KB)
+    static constexpr int W_CHUNK = kDcBlocks * 512;               // packed words of one chunk of a group (8 KB)
     static constexpr int W_BYTES = kDcStep * W_CHUNK;             // [chunk][n16 block][32 lanes x 16 B]
     static constexpr int X_CHUNK = MP * 128;                      // one chunk's token rows (128-byte swizzle)
     static constexpr int X_BYTES = kDcStep * X_CHUNK;
@@ -96,7 +101,7 @@ struct DcPartition {
 
 __host__ __device__ inline DcPartition dc_partition(int N, int K, int num_sms) {
     DcPartition p;
-    p.groups = (N / 16 + kDcWarps - 1) / kDcWarps;
+    p.groups = (N / 16 + kDcBlocks - 1) / kDcBlocks;
     p.kc = K / 64;
     const long long total = (long long)p.groups * p.kc;
     p.valid = total > 0 && total < (1ll << 31);
@@ -184,7 +189,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         auto issue_weights = [&](int s, const DcSteps& w, int nk) {   // packed words + scales
             mbar_expect_tx(full(s), (uint32_t)nk * (w_bytes + s_bytes));
             for (int j = 0; j < nk; ++j) {
-                tma_load_3d(stage(s) + j * C::W_CHUNK, &tw, 0, w.kc + j, w.g * kDcWarps, full(s));
+                tma_load_3d(stage(s) + j * C::W_CHUNK, &tw, 0, w.kc + j, w.g * kDcBlocks, full(s));
                 tma_load_2d(stage(s) + C::W_BYTES + C::X_BYTES + j * C::SROW, &ts, w.g * kDcCols,
                             ((w.kc + j) * 64) / G, full(s));
             }
@@ -223,54 +228,62 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         return;
     }
 
-    // ---------------------------------------------------- consumer warp: n16 block `warp` of each group
+    // ---------------------------------------------------- consumer warp: n16 blocks warp*BPW.. of each group
+    constexpr int BPW = kDcBPW;
+    constexpr int CH = kDcStep / BPW > 0 ? kDcStep / BPW : 1;     // accumulator chains per block
     const int g8 = lane >> 2, t4 = lane & 3;
     pdl_wait();   // the workspace and y may still be in use by the previous kernel
     pdl_launch_dependents();
 
-    const uint32_t w_lane = (uint32_t)(warp * 512 + lane * 16);
+    const uint32_t w_lane = (uint32_t)(warp * BPW * 512 + lane * 16);
     // ldmatrix row addresses in a 128-byte-swizzled chunk of token rows: row r's 16-byte unit u
     // sits at unit u ^ (r % 8); lanes 8i..8i+7 address rows 0..7 of 8x8 matrix i (k units i, i+4)
     const uint32_t xr = (uint32_t)(lane & 7), xu = (uint32_t)(lane >> 3);
     const uint32_t x_lane0 = C::W_BYTES + xr * 128 + ((xu ^ xr) << 4);
     const uint32_t x_lane1 = C::W_BYTES + xr * 128 + (((xu + 4) ^ xr) << 4);
-    const uint32_t s_lane = (uint32_t)(C::W_BYTES + C::X_BYTES + warp * 32 + g8 * 2);
+    const uint32_t s_lane = (uint32_t)(C::W_BYTES + C::X_BYTES + warp * BPW * 32 + g8 * 2);
 
-    float acc[kDcStep][MT][4];
+    float acc[BPW][CH][MT][4];
 #pragma unroll
-    for (int j = 0; j < kDcStep; ++j)
+    for (int bb = 0; bb < BPW; ++bb)
 #pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
+        for (int ch = 0; ch < CH; ++ch)
 #pragma unroll
-            for (int i = 0; i < 4; ++i) acc[j][mt][i] = 0.f;
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+                for (int i = 0; i < 4; ++i) acc[bb][ch][mt][i] = 0.f;
 
     DcSteps st;
     st.start(c0, c1, KC);
     int gkc0 = st.kc;                 // first chunk of the current group inside this CTA
     for (int t = 0; st.more(); ++t) {
         const int nk = st.nk(KC), s = t % ST;
-        const bool active = st.g * kDcWarps + warp < NB;
+        const int nb0 = st.g * kDcBlocks + warp * BPW;      // this warp's first n16 block
         if (!__all_sync(0xffffffffu, mbar_wait_sleep(full(s), (t / ST) & 1, kDevTimeoutWeights))) break;
-        if (active) {
+        if (nb0 < NB) {
             const uint32_t sb = stage(s);
-            // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are 0 too)
-            uint32_t s_lo[kDcStep], s_hi[kDcStep];
+            // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are finite)
+            uint32_t s_lo[BPW][kDcStep], s_hi[BPW][kDcStep];
 #pragma unroll
-            for (int j = 0; j < kDcStep; ++j) {
-                const uint16_t lo = lds_u16(sb + s_lane + j * C::SROW);
-                const uint16_t hi = lds_u16(sb + s_lane + j * C::SROW + 16);
-                s_lo[j] = j < nk ? bcast_half(lo) : 0u;
-                s_hi[j] = j < nk ? bcast_half(hi) : 0u;
-            }
+            for (int bb = 0; bb < BPW; ++bb)
+#pragma unroll
+                for (int j = 0; j < kDcStep; ++j) {
+                    const uint32_t sa = sb + s_lane + bb * 32 + j * C::SROW;
+                    const uint16_t lo = lds_u16(sa);
+                    const uint16_t hi = lds_u16(sa + 16);
+                    s_lo[bb][j] = j < nk ? bcast_half(lo) : 0u;
+                    s_hi[bb][j] = j < nk ? bcast_half(hi) : 0u;
+                }
             const uint32_t wb = sb + w_lane;
-            constexpr int JB = MT == 1 ? 4 : 2;
+            constexpr int JB = MT == 1 ? 4 / (BPW > 2 ? 2 : 1) : (BPW > 1 ? 1 : 2);
 #pragma unroll
             for (int jb = 0; jb < kDcStep; jb += JB) {
-                uint4 wv[JB];
+                uint4 wv[JB][BPW];
                 uint32_t b[JB][MT][8];
 #pragma unroll
                 for (int jj = 0; jj < JB; ++jj) {
-                    wv[jj] = lds128(wb + (jb + jj) * C::W_CHUNK);
+#pragma unroll
+                    for (int bb = 0; bb < BPW; ++bb) wv[jj][bb] = lds128(wb + (jb + jj) * C::W_CHUNK + bb * 512);
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
                         const uint32_t xa = sb + (jb + jj) * C::X_CHUNK + mt * 1024;
@@ -278,18 +291,22 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                         ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][4]), xa + x_lane1);
                     }
                 }
-                // No per-chunk guard: the unconditional body lets the 4 accumulator chains interleave.
+                // No per-chunk guard: the unconditional body lets the accumulator chains interleave.
+                // The activation fragments of a chunk serve all BPW blocks.
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
-                    for (int jj = 0; jj < JB; ++jj) {
-                        const uint32_t wq = ks == 0 ? wv[jj].x : ks == 1 ? wv[jj].y : ks == 2 ? wv[jj].z : wv[jj].w;
-                        uint32_t a[4];
-                        dequant_word(wq, s_lo[jb + jj], s_hi[jb + jj], a);
+                    for (int jj = 0; jj < JB; ++jj)
 #pragma unroll
-                        for (int mt = 0; mt < MT; ++mt)
-                            mma_16816(acc[jb + jj][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);
-                    }
+                        for (int bb = 0; bb < BPW; ++bb) {
+                            const uint4 w4 = wv[jj][bb];
+                            const uint32_t wq = ks == 0 ? w4.x : ks == 1 ? w4.y : ks == 2 ? w4.z : w4.w;
+                            uint32_t a[4];
+                            dequant_word(wq, s_lo[bb][jb + jj], s_hi[bb][jb + jj], a);
+#pragma unroll
+                            for (int mt = 0; mt < MT; ++mt)
+                                mma_16816(acc[bb][(jb + jj) % CH][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);
+                        }
             }
         }
         // release the stage to the producer
@@ -298,10 +315,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         const int g = st.g;
         const bool whole_end = st.kc + nk == KC && gkc0 == 0;
         if (st.advance(nk, KC)) {
-            // this CTA's part of group g is done: fold the 4 chains (fixed order) and store
-            if (active) {
-                const int col = g * kDcCols + warp * 16 + g8;
-                float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats + warp * 16 + g8;
+            // this CTA's part of group g is done: fold the chains (fixed order) and store
+#pragma unroll
+            for (int bb = 0; bb < BPW; ++bb) {
+                const int nb = g * kDcBlocks + warp * BPW + bb;
+                const int colb = (warp * BPW + bb) * 16 + g8;           // column inside the group
+                float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats + colb;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -309,15 +328,16 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                         const int tok = mt * 8 + 2 * t4 + (i & 1);
                         float v = 0.f;
 #pragma unroll
-                        for (int j = 0; j < kDcStep; ++j) {
-                            v += acc[j][mt][i];
-                            acc[j][mt][i] = 0.f;
+                        for (int ch = 0; ch < CH; ++ch) {
+                            v += acc[bb][ch][mt][i];
+                            acc[bb][ch][mt][i] = 0.f;
                         }
-                        if (tok < M) {
+                        if (nb < NB && tok < M) {
                             const int dc = 8 * (i >> 1);
                             if (whole_end) {
-                                if (OUT_F32) static_cast<float*>(yv)[(size_t)tok * N + col + dc] = v;
-                                else static_cast<__half*>(yv)[(size_t)tok * N + col + dc] = __float2half_rn(v);
+                                const size_t o = (size_t)tok * N + g * kDcCols + colb + dc;
+                                if (OUT_F32) static_cast<float*>(yv)[o] = v;
+                                else static_cast<__half*>(yv)[o] = __float2half_rn(v);
                             } else {
                                 __stcg(my + tok * kDcCols + dc, v);
                             }
@@ -399,12 +419,12 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     if ((err = device_info(&dev)) != cudaSuccess) return err;
     const DcPartition part = dc_partition(a.N, a.K, dev.num_sms);
     float* partials = static_cast<float*>(a.workspace);
-    const int box_blocks = std::min(kDcWarps, a.N / 16);
+    const int box_blocks = std::min(kDcBlocks, a.N / 16);
     CUtensorMap tw, tx, ts;
     if ((err = make_decode_tensor_maps(a, box_blocks, MP, &tw, &tx, &ts)) != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(part.ctas, 1, 1);
-    cfg.blockDim = dim3(kDcThreads, 1, 1);   // 16 consumer warps + 1 producer warp
+    cfg.blockDim = dim3(kDcThreads, 1, 1);   // consumer warps + 1 producer warp
     cfg.dynamicSmemBytes = DcCfg<MP>::SMEM;
     cfg.stream = a.stream;
     cudaLaunchAttribute attr;
