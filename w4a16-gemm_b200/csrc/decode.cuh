@@ -8,29 +8,27 @@
 //   * Output columns form groups of 256 (16 n16 blocks).  The work is the
 //     sequence of (group, 64-wide K chunk) pairs, group-major, cut into equal
 //     contiguous ranges, one per SM (stream-K): every SM moves the same number
-//     of packed-word bytes (to one chunk) whatever N and K are.
-//   * One persistent CTA per SM: 16 consumer warps + 1 producer warp.  A CTA
-//     walks its range in steps of up to 4 chunks inside one group.  Consumer
-//     warp w owns n16 block w of the group: its packed words for a step are
-//     one contiguous run (<= 2 KB), streamed through a private ring of 1-D
-//     bulk copies that the warp issues itself -- the copy engine services one
-//     warp's requests one after another (measured), so 16 issuing warps per
-//     SM are what reaches HBM bandwidth.
-//   * The producer warp stages each step's activation rows (M x 512 B, rows
-//     528 B apart so ldmatrix reads them conflict-free) and the group's scale
-//     rows (512 B each) with 16-byte cp.async into a ring of stages shared by
-//     all 16 consumers; mbarriers carry full / empty hand-offs, so consumer
-//     warps never wait on one another.
-//   * The packed word of each lane is already an m16n8k16 A fragment, so the
-//     exact 13-instruction dequant feeds mma.sync directly (weights = A, the
-//     <= 16 tokens = the n8 side); 4 independent fp32 accumulator chains.
-//   * Each warp's columns are complete in its own registers when the CTA
-//     leaves a group: a group covered by one CTA is written to y directly; a
-//     group split across CTAs leaves one fp32 partial per CTA in the caller's
-//     workspace and decode_fixup_kernel (launched behind with programmatic
-//     dependent launch) sums them in CTA order -- deterministic, no atomics.
-//   * Programmatic dependent launch: the first packed-word copies are issued
-//     before griddepcontrol.wait (weights never depend on the previous kernel).
+//     of packed-word bytes (to one chunk) whatever N and K are.  Small GEMMs use
+//     fewer CTAs (at least kDcMinUnits chunks each) so fewer partials are combined.
+//   * One CTA per SM: 8 consumer warps + 1 producer warp.  A CTA walks its range
+//     in steps of up to kDcStep chunks inside one group.  One producer lane
+//     issues each step as tensor copies (TMA) onto the stage's single mbarrier:
+//     the packed words of the group's 16 n16 blocks in ONE box -- for each block
+//     its kDcStep chunks are one contiguous run in HBM (2 KB), which DRAM serves
+//     far better than 512-byte pieces -- the token rows of the step's chunks in
+//     one box (128-byte swizzle, rows >= M zero-filled) and the group's scales.
+//   * Consumer warp w owns n16 blocks 2w and 2w+1 of the group.  The packed word
+//     of each lane is already an m16n8k16 A fragment, so the exact
+//     13-instruction dequant feeds mma.sync directly (weights = A, the <= 16
+//     tokens = the n8 side); one activation fragment serves both blocks.
+//   * A CTA's columns are complete in registers when it leaves a group: a group
+//     covered by one CTA is written to y directly; a group split across CTAs
+//     leaves one fp32 partial per CTA in the caller's workspace, and
+//     decode_combine_kernel (launched behind with programmatic dependent launch)
+//     sums them in CTA order -- deterministic, no atomics, no counters.
+//   * Programmatic dependent launch: the first ring stages of packed words and
+//     scales are issued before griddepcontrol.wait (weights never depend on the
+//     previous kernel); dependents may launch as soon as every CTA has started.
 #pragma once
 #include <cuda.h>
 #include <cuda_fp16.h>
@@ -45,24 +43,25 @@
 namespace w4a16 {
 
 constexpr int kDcBlocks = 16;                             // n16 blocks per group
-#ifndef W4A16_DC_BPW
-#define W4A16_DC_BPW 2
-#endif
-constexpr int kDcBPW = W4A16_DC_BPW;                      // n16 blocks per consumer warp
-constexpr int kDcWarps = kDcBlocks / kDcBPW;              // consumer warps; warp w owns blocks w*BPW.. of a group
+constexpr int kDcBPW = 2;                                 // n16 blocks per consumer warp
+constexpr int kDcWarps = kDcBlocks / kDcBPW;              // consumer warps; warp w owns blocks 2w, 2w+1
 constexpr int kDcThreads = (kDcWarps + 1) * 32;           // + the producer warp
 constexpr int kDcCols = kDcBlocks * 16;                   // output columns per group
 constexpr int kDcStep = 4;                                // 64-wide K chunks per step
 constexpr int kDcSlotFloats = 16 * kDcCols;               // one partial: 16 tokens x 256 columns
 constexpr int kDcMaxCTAs = 1024;
+// Fewest (group, chunk) units a CTA gets: a small GEMM runs on fewer CTAs rather than
+// splitting each column group over dozens of them (its copies are all in flight at once
+// either way, and the combine reads fewer partials).
+constexpr int kDcMinUnits = 4;
 
 template <int MP>
 struct DcCfg {
-    static constexpr int ST = 4;                                  // stages: steps in flight
+    static constexpr int ST = 5;                                  // stages: steps in flight
     static constexpr int W_CHUNK = kDcBlocks * 512;               // packed words of one chunk of a group (8 KB)
-    static constexpr int W_BYTES = kDcStep * W_CHUNK;             // [chunk][n16 block][32 lanes x 16 B]
+    static constexpr int W_BYTES = kDcStep * W_CHUNK;             // [n16 block][chunk][32 lanes x 16 B]
     static constexpr int X_CHUNK = MP * 128;                      // one chunk's token rows (128-byte swizzle)
-    static constexpr int X_BYTES = kDcStep * X_CHUNK;
+    static constexpr int X_BYTES = kDcStep * X_CHUNK;             // [chunk][token row][128 B]
     static constexpr int SROW = kDcCols * 2;                      // one chunk's scales of the group (512 B)
     static constexpr int S_BYTES = kDcStep * SROW;
     static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + S_BYTES;
@@ -80,20 +79,17 @@ struct DcPartition {
     int ctas;      // CTAs (<= total)
     bool valid;    // total fits 32 bits
     __host__ __device__ int c0(int c) const { return (int)(((long long)c * total) / ctas); }
-    // First / last CTA whose range intersects group g.
+    // First / last CTA whose range intersects group g (closed forms of "largest c with
+    // c0(c) <= g*kc" and "largest c with c0(c) < (g+1)*kc"; one division each).
     __host__ __device__ int first_cta(int g) const {
-        const long long lo = (long long)g * kc;
-        int c = (int)((lo * ctas) / total);
-        while (c > 0 && c0(c) > lo) --c;
-        while (c0(c + 1) <= lo) ++c;
-        return c;
+        const unsigned long long lo = (unsigned long long)g * kc;
+        const int c = (int)(((lo + 1) * (unsigned)ctas - 1) / (unsigned)total);
+        return c < ctas - 1 ? c : ctas - 1;
     }
     __host__ __device__ int last_cta(int g) const {
-        const long long hi = (long long)(g + 1) * kc;      // exclusive
-        int c = (int)(((hi - 1) * ctas) / total);
-        while (c + 1 < ctas && c0(c + 1) < hi) ++c;
-        while (c0(c) >= hi) --c;
-        return c;
+        const unsigned long long hi = (unsigned long long)(g + 1) * kc;
+        const int c = (int)((hi * (unsigned)ctas - 1) / (unsigned)total);
+        return c < ctas - 1 ? c : ctas - 1;
     }
     // Workspace slot of CTA c's partial of group g (only for split groups).
     __host__ __device__ int slot(int c, int g) const { return 2 * c + (g == c0(c) / kc ? 0 : 1); }
@@ -106,7 +102,8 @@ __host__ __device__ inline DcPartition dc_partition(int N, int K, int num_sms) {
     const long long total = (long long)p.groups * p.kc;
     p.valid = total > 0 && total < (1ll << 31);
     p.total = p.valid ? (int)total : 1;
-    p.ctas = num_sms < p.total ? num_sms : p.total;
+    const int cap = p.total / kDcMinUnits > 0 ? p.total / kDcMinUnits : 1;
+    p.ctas = num_sms < cap ? num_sms : cap;
     if (p.ctas > kDcMaxCTAs) p.ctas = kDcMaxCTAs;
     return p;
 }
@@ -119,10 +116,10 @@ __host__ __device__ inline bool dc_has_split(const DcPartition& p) {
 }
 
 // Workspace: 2 fp32 partial slots per CTA (a CTA's range splits at most its first
-// and its last group).  Always fully written before it is read; no initial contents
-// are assumed.
+// and its last group), only when some group is split.  Always fully written before
+// it is read; no initial contents are assumed.
 __host__ __device__ inline size_t dc_workspace_bytes(const DcPartition& p) {
-    return (size_t)2 * p.ctas * kDcSlotFloats * 4;
+    return dc_has_split(p) ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
 }
 
 // Walks a CTA's chunk range [pos, end) in steps of <= kDcStep chunks that never
@@ -145,7 +142,7 @@ template <int G, int MP, bool OUT_F32>
 __global__ void __launch_bounds__(kDcThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
               const __grid_constant__ CUtensorMap ts, void* __restrict__ yv, int M, int N, int box_blocks,
-              DcPartition part, float* __restrict__ partials)
+              int box_chunks, DcPartition part, float* __restrict__ partials)
 {
     using C = DcCfg<MP>;
     constexpr int ST = C::ST;
@@ -153,13 +150,16 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
     extern __shared__ uint8_t smem_raw[];
     const uint32_t raw = smem_u32(smem_raw);
     const uint32_t base = (raw + 1023u) & ~1023u;
-    uint8_t* const gbase = smem_raw + (base - raw);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
     const uint32_t bars = base + ST * C::STAGE_BYTES;
     auto stage = [&](int s) { return base + (uint32_t)s * C::STAGE_BYTES; };
     auto full = [&](int s) { return bars + (uint32_t)s * 8; };
     auto empty = [&](int s) { return bars + (uint32_t)(ST + s) * 8; };
+
+    // The next kernel may launch as soon as every CTA of this one has started: it only
+    // prepares and streams weights until its own griddepcontrol.wait releases it.
+    pdl_launch_dependents();
 
     const int c = blockIdx.x;
     const int c0 = part.c0(c), c1 = part.c0(c + 1);
@@ -172,27 +172,34 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         }
     }
     fence_mbar_init();
-    // Token rows start zeroed: chunks a step does not load keep finite contents (zeros or
-    // earlier activations), which their zero scales cancel.
-    for (int s = 0; s < ST; ++s)
-        for (int i = threadIdx.x; i < C::X_BYTES / 16; i += kDcThreads)
-            reinterpret_cast<uint4*>(gbase + s * C::STAGE_BYTES + C::W_BYTES)[i] = make_uint4(0, 0, 0, 0);
+    if (box_chunks < kDcStep) {
+        // K < 256: a step's token-row box covers fewer than kDcStep chunks and the rest of the
+        // stage's rows are never written; zero them once so those chunks (whose scales are
+        // zero) multiply finite values.
+        uint8_t* const gbase = smem_raw + (base - raw);
+        for (int s = 0; s < ST; ++s)
+            for (int i = threadIdx.x; i < C::X_BYTES / 16; i += kDcThreads)
+                reinterpret_cast<uint4*>(gbase + s * C::STAGE_BYTES + C::W_BYTES)[i] = make_uint4(0, 0, 0, 0);
+        fence_proxy_async_smem();   // the zeros land before any tensor copy into the same rows
+    }
     __syncthreads();
 
     if (warp == kDcWarps) {
         // ------------------------------------------------ producer (one lane): all of a step by tensor copies
-        // Per chunk j of a step: the packed words of up to 16 n16 blocks (box 16 x 512 B; blocks
-        // beyond N zero-filled) into [chunk][block][512 B]; the token rows (box 64 x MP fp16,
-        // rows >= M zero-filled, 128-byte swizzle); the group's scales of the chunk (box 256 x 1).
+        // Per step: the packed words of up to 16 n16 blocks x box_chunks chunks in one box into
+        // [block][chunk][512 B] (chunks past K and blocks past N zero-filled); the token rows of
+        // the step's chunks (box 64 x MP x box_chunks, rows >= M zero-filled, 128-byte swizzle)
+        // into [chunk][row][128 B]; per chunk the group's scales (box 256 x 1).  Chunks of a box
+        // past the step's nk are loaded but their scales stay zero, so they add nothing.
         if (lane != 0) return;
-        const uint32_t w_bytes = (uint32_t)box_blocks * 512, s_bytes = (uint32_t)(box_blocks * 16 * 2);
+        const uint32_t w_bytes = (uint32_t)(box_blocks * box_chunks * 512), s_bytes = (uint32_t)(box_blocks * 16 * 2);
+        const uint32_t x_bytes = (uint32_t)(box_chunks * C::X_CHUNK);
         auto issue_weights = [&](int s, const DcSteps& w, int nk) {   // packed words + scales
-            mbar_expect_tx(full(s), (uint32_t)nk * (w_bytes + s_bytes));
-            for (int j = 0; j < nk; ++j) {
-                tma_load_3d(stage(s) + j * C::W_CHUNK, &tw, 0, w.kc + j, w.g * kDcBlocks, full(s));
+            mbar_expect_tx(full(s), w_bytes + (uint32_t)nk * s_bytes);
+            tma_load_3d(stage(s), &tw, 0, w.kc, w.g * kDcBlocks, full(s));
+            for (int j = 0; j < nk; ++j)
                 tma_load_2d(stage(s) + C::W_BYTES + C::X_BYTES + j * C::SROW, &ts, w.g * kDcCols,
                             ((w.kc + j) * 64) / G, full(s));
-            }
         };
         DcSteps st;
         st.start(c0, c1, KC);
@@ -208,7 +215,6 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
             }
         }
         pdl_wait();   // x may still be written by the previous kernel
-        pdl_launch_dependents();
         int t = 0;
         for (; st.more(); ++t) {
             const int nk = st.nk(KC), s = t % ST;
@@ -216,9 +222,8 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                 if (!mbar_wait_sleep(empty(s), ((t / ST) - 1) & 1, kDevTimeoutActivations)) break;
                 issue_weights(s, st, nk);
             }
-            mbar_arrive_expect_tx(full(s), (uint32_t)(nk * C::X_CHUNK));
-            for (int j = 0; j < nk; ++j)
-                tma_load_2d(stage(s) + C::W_BYTES + j * C::X_CHUNK, &tx, (st.kc + j) * 64, 0, full(s));
+            mbar_arrive_expect_tx(full(s), x_bytes);
+            tma_load_3d(stage(s) + C::W_BYTES, &tx, 0, 0, st.kc, full(s));
             st.advance(nk, KC);
         }
         // Tensor copies still in flight must land before the CTA may exit: normally the last ST
@@ -228,14 +233,14 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         return;
     }
 
-    // ---------------------------------------------------- consumer warp: n16 blocks warp*BPW.. of each group
+    // ---------------------------------------------------- consumer warp: n16 blocks 2*warp, 2*warp+1 of each group
     constexpr int BPW = kDcBPW;
-    constexpr int CH = kDcStep / BPW > 0 ? kDcStep / BPW : 1;     // accumulator chains per block
+    constexpr int CH = 2;                                          // accumulator chains per block
     const int g8 = lane >> 2, t4 = lane & 3;
     pdl_wait();   // the workspace and y may still be in use by the previous kernel
-    pdl_launch_dependents();
 
-    const uint32_t w_lane = (uint32_t)(warp * BPW * 512 + lane * 16);
+    const uint32_t w_blk = (uint32_t)box_chunks * 512;            // block stride of a stage's packed words
+    const uint32_t w_lane = (uint32_t)warp * BPW * w_blk + lane * 16;
     // ldmatrix row addresses in a 128-byte-swizzled chunk of token rows: row r's 16-byte unit u
     // sits at unit u ^ (r % 8); lanes 8i..8i+7 address rows 0..7 of 8x8 matrix i (k units i, i+4)
     const uint32_t xr = (uint32_t)(lane & 7), xu = (uint32_t)(lane >> 3);
@@ -275,7 +280,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                     s_hi[bb][j] = j < nk ? bcast_half(hi) : 0u;
                 }
             const uint32_t wb = sb + w_lane;
-            constexpr int JB = MT == 1 ? 4 / (BPW > 2 ? 2 : 1) : (BPW > 1 ? 1 : 2);
+            constexpr int JB = MT == 1 ? 4 : 1;                // chunks whose operands are loaded together
 #pragma unroll
             for (int jb = 0; jb < kDcStep; jb += JB) {
                 uint4 wv[JB][BPW];
@@ -283,7 +288,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
 #pragma unroll
                 for (int jj = 0; jj < JB; ++jj) {
 #pragma unroll
-                    for (int bb = 0; bb < BPW; ++bb) wv[jj][bb] = lds128(wb + (jb + jj) * C::W_CHUNK + bb * 512);
+                    for (int bb = 0; bb < BPW; ++bb) wv[jj][bb] = lds128(wb + (jb + jj) * 512 + bb * w_blk);
 #pragma unroll
                     for (int mt = 0; mt < MT; ++mt) {
                         const uint32_t xa = sb + (jb + jj) * C::X_CHUNK + mt * 1024;
@@ -292,7 +297,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                     }
                 }
                 // No per-chunk guard: the unconditional body lets the accumulator chains interleave.
-                // The activation fragments of a chunk serve all BPW blocks.
+                // The activation fragments of a chunk serve both blocks.
 #pragma unroll
                 for (int ks = 0; ks < 4; ++ks)
 #pragma unroll
@@ -313,14 +318,14 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         __syncwarp();
         if (lane == 0) mbar_arrive(empty(s));
         const int g = st.g;
-        const bool whole_end = st.kc + nk == KC && gkc0 == 0;
+        const bool whole = st.kc + nk == KC && gkc0 == 0;
         if (st.advance(nk, KC)) {
             // this CTA's part of group g is done: fold the chains (fixed order) and store
+            float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats;
 #pragma unroll
             for (int bb = 0; bb < BPW; ++bb) {
                 const int nb = g * kDcBlocks + warp * BPW + bb;
                 const int colb = (warp * BPW + bb) * 16 + g8;           // column inside the group
-                float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats + colb;
 #pragma unroll
                 for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -334,12 +339,12 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                         }
                         if (nb < NB && tok < M) {
                             const int dc = 8 * (i >> 1);
-                            if (whole_end) {
+                            if (whole) {
                                 const size_t o = (size_t)tok * N + g * kDcCols + colb + dc;
                                 if (OUT_F32) static_cast<float*>(yv)[o] = v;
                                 else static_cast<__half*>(yv)[o] = __float2half_rn(v);
                             } else {
-                                __stcg(my + tok * kDcCols + dc, v);
+                                __stcg(my + tok * kDcCols + colb + dc, v);
                             }
                         }
                     }
@@ -351,13 +356,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
 
 // Combines the groups that the stream-K partition split across CTAs: one CTA per
 // (group, token); groups owned by a single CTA were written by decode_kernel already.
-// Launched right behind decode_kernel with programmatic dependent launch, so it
-// is resident early and griddepcontrol.wait releases it when decode_kernel's
-// writes are complete and visible.  Sums the partials in CTA order; the loads of
+// Launched right behind decode_kernel with programmatic dependent launch, so it is
+// resident early and griddepcontrol.wait releases it once decode_kernel's writes are
+// complete and visible.  Sums the partials in CTA order (deterministic); the loads of
 // 8 partials are issued together so the sum is not one serial chain of L2 trips.
 template <bool OUT_F32>
-__global__ void __launch_bounds__(kDcCols) decode_fixup_kernel(void* __restrict__ yv, int N, DcPartition part,
-                                                               const float* __restrict__ partials) {
+__global__ void __launch_bounds__(kDcCols) decode_combine_kernel(void* __restrict__ yv, int N, DcPartition part,
+                                                                 const float* __restrict__ partials) {
     const int g = blockIdx.x, tok = blockIdx.y;
     const int cf = part.first_cta(g), cl = part.last_cta(g);
     pdl_launch_dependents();
@@ -405,13 +410,14 @@ size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev) {
 }
 
 // Tensor maps of the decode kernel (kernels.cu): packed words viewed as [NB][KC][128] int32,
-// box {128, 1, box_blocks} (one 64-wide chunk of up to 16 n16 blocks); x [M, K] fp16, box
-// {64, MP} with 128-byte swizzle; scales [K/G, N] fp16, box {16 * box_blocks, 1}.
-cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int mp, CUtensorMap* tw, CUtensorMap* tx,
-                                    CUtensorMap* ts);
+// box {128, box_chunks, box_blocks}; x viewed as [KC][M][64] fp16, box {64, MP, box_chunks}
+// with 128-byte swizzle; scales [K/G, N] fp16, box {16 * box_blocks, 1}.
+cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int box_chunks, int mp, CUtensorMap* tw,
+                                    CUtensorMap* tx, CUtensorMap* ts);
 
 template <int G, int MP, bool F32>
 static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
+    (void)p;
     auto kern = decode_kernel<G, MP, F32>;
     cudaError_t err = ensure_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (err != cudaSuccess) return err;
@@ -420,8 +426,9 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     const DcPartition part = dc_partition(a.N, a.K, dev.num_sms);
     float* partials = static_cast<float*>(a.workspace);
     const int box_blocks = std::min(kDcBlocks, a.N / 16);
+    const int box_chunks = std::min(kDcStep, a.K / 64);
     CUtensorMap tw, tx, ts;
-    if ((err = make_decode_tensor_maps(a, box_blocks, MP, &tw, &tx, &ts)) != cudaSuccess) return err;
+    if ((err = make_decode_tensor_maps(a, box_blocks, box_chunks, MP, &tw, &tx, &ts)) != cudaSuccess) return err;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(part.ctas, 1, 1);
     cfg.blockDim = dim3(kDcThreads, 1, 1);   // consumer warps + 1 producer warp
@@ -432,7 +439,7 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
-    err = cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, part, partials);
+    err = cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, box_chunks, part, partials);
     if (err != cudaSuccess || !dc_has_split(part)) return err;
     // combine split groups; always launched programmatically dependent on decode_kernel
     cudaLaunchConfig_t fc = {};
@@ -444,7 +451,7 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     fattr.val.programmaticStreamSerializationAllowed = 1;
     fc.attrs = &fattr;
     fc.numAttrs = 1;
-    return cudaLaunchKernelEx(&fc, decode_fixup_kernel<F32>, a.y, a.N, part, static_cast<const float*>(partials));
+    return cudaLaunchKernelEx(&fc, decode_combine_kernel<F32>, a.y, a.N, part, static_cast<const float*>(partials));
 }
 
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p) {

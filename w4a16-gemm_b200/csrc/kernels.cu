@@ -50,6 +50,9 @@ cudaError_t ensure_max_dynamic_smem(const void* func) {
     std::lock_guard<std::mutex> lk(mu);
     if (done.count({func, d.device})) return cudaSuccess;
     err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin);
+    // all of the unified L1/shared array as shared memory (the kernels stage through it)
+    if (err == cudaSuccess)
+        err = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
     if (err == cudaSuccess) done.insert({func, d.device});
     return err;
 }
@@ -123,25 +126,27 @@ cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx
     return cudaSuccess;
 }
 
-cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int mp, CUtensorMap* tw, CUtensorMap* tx,
-                                    CUtensorMap* ts) {
+cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int box_chunks, int mp, CUtensorMap* tw,
+                                    CUtensorMap* tx, CUtensorMap* ts) {
     auto encode = tensor_map_encoder();
     if (!encode) return cudaErrorNotSupported;
     const cuuint32_t one[3] = {1, 1, 1};
-    {   // packed words [NB][KC][128] int32, box {128, 1, box_blocks}
+    {   // packed words [NB][KC][128] int32, box {128, box_chunks, box_blocks}: per n16 block one
+        // contiguous run of box_chunks * 512 bytes
         const cuuint64_t dims[3] = {128, (cuuint64_t)(a.K / 64), (cuuint64_t)(a.N / 16)};
         const cuuint64_t strides[2] = {512, (cuuint64_t)(a.K / 64) * 512};
-        const cuuint32_t box[3] = {128, 1, (cuuint32_t)box_blocks};
+        const cuuint32_t box[3] = {128, (cuuint32_t)box_chunks, (cuuint32_t)box_blocks};
         if (encode(tw, CU_TENSOR_MAP_DATA_TYPE_INT32, 3, const_cast<void*>(a.wp), dims, strides, box, one,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
     }
-    {   // x [M, K] fp16, box {64, mp} (rows >= M read as zeros), 128-byte swizzle
-        const cuuint64_t dims[2] = {(cuuint64_t)a.K, (cuuint64_t)a.M};
-        const cuuint64_t strides[1] = {(cuuint64_t)a.K * 2};
-        const cuuint32_t box[2] = {64, (cuuint32_t)mp};
-        if (encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(a.x), dims, strides, box, one,
+    {   // x [M, K] fp16 viewed as [K/64][M][64], box {64, mp, box_chunks} (rows >= M and chunks
+        // past K read as zeros), 128-byte swizzle
+        const cuuint64_t dims[3] = {64, (cuuint64_t)a.M, (cuuint64_t)(a.K / 64)};
+        const cuuint64_t strides[2] = {(cuuint64_t)a.K * 2, 128};
+        const cuuint32_t box[3] = {64, (cuuint32_t)mp, (cuuint32_t)box_chunks};
+        if (encode(tx, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(a.x), dims, strides, box, one,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
             return cudaErrorInvalidValue;
