@@ -14,13 +14,14 @@
 // exactly that fragment order.  Shared memory only carries the TMA-loaded x
 // tile (128-byte swizzle), the raw packed words and one scale row per stage.
 //
-// Warp roles (448 threads, one CTA per SM, all 512 TMEM columns):
+// Warp roles (one CTA per SM, all 512 TMEM columns):
 //   warp 0      TMA producer: x tile [TOK x 64] (SW128), packed words of 8 n16
 //               blocks for one 64-wide K chunk (3-D tensor map), 128 scales
 //   warp 1      TMEM allocator + single-thread tcgen05.mma issuer
-//   warps 2-9   dequant: warp w owns n16 block 2*(w%4) + (w>=6) of the tile,
-//               i.e. TMEM lanes inside its own lane quarter
-//   warps 10-13 epilogue: tcgen05.ld of the accumulator, fp16/fp32 stores
+//   warps 2..   dequant (kPfDqPhases groups of 8): warp w owns n16 block
+//               2*(w%4) + ((w-2)/4 & 1) of the tile, i.e. TMEM lanes inside its own
+//               lane quarter, for the k-steps of its group ((w-2)/8)
+//   last 4      epilogue: tcgen05.ld of the accumulator, fp16/fp32 stores
 //
 // K is walked in one sequential order for every tile shape, so all prefill
 // configs (TOK = 32/64/128/256) give bit-identical results and a row's output
@@ -39,7 +40,15 @@
 
 namespace w4a16 {
 
-constexpr int kPfThreads = 14 * 32;
+#ifndef W4A16_PF_DQ_PHASES
+#define W4A16_PF_DQ_PHASES 1
+#endif
+// Dequant warp groups: group p (8 warps, one per n16 block of the tile) takes the k-steps
+// it with it % kPfDqPhases == p, so consecutive k-steps are dequantised concurrently.
+constexpr int kPfDqPhases = W4A16_PF_DQ_PHASES;
+constexpr int kPfDqWarps = 8 * kPfDqPhases;
+constexpr int kPfEpiWarp0 = 2 + kPfDqWarps;   // first of the 4 epilogue warps
+constexpr int kPfThreads = (kPfEpiWarp0 + 4) * 32;
 constexpr int kPfRows = 128;                 // output channels per tile (UMMA M)
 constexpr int kPfWBytes = 8 * 512;           // packed words: 8 n16 blocks x one 64-k chunk
 constexpr int kPfSBytes = kPfRows * 2;       // one fp16 scale row slice
@@ -191,15 +200,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             tc_commit(done_bar);   // every MMA of this CTA retired before TMEM is released
             mbar_wait(done_bar, 0, kDevTimeoutDrain);
         }
-    } else if (warp < 10) {
+    } else if (warp < kPfEpiWarp0) {
         // ------------------------------------------------------------ dequant -> TMEM A ring
-        const int nbl = 2 * (warp & 3) + (warp >= 6 ? 1 : 0);   // n16 block inside the tile
+        const int qi = (warp - 2) >> 2;                             // index among this quarter's warps
+        const int nbl = 2 * (warp & 3) + (qi & 1);                  // n16 block inside the tile
+        const int phase = qi >> 1;                                  // k-steps it % kPfDqPhases == phase
         const int g = lane >> 2;
         const uint32_t lane_field = (uint32_t)(16 * nbl) << 16;
         int it = 0;
         bool ok = true;
         for (int tile = blockIdx.x; tile < total && ok; tile += gridDim.x) {
             for (int kt = 0; kt < KT; ++kt, ++it) {
+                if (it % kPfDqPhases != phase) continue;
                 const int s = it % ST, a = it % NA;
                 bool w_ok = mbar_wait(full(s), (it / ST) & 1, kDevTimeoutPipeline);
                 w_ok = w_ok && mbar_wait(aempty(a), ((it / NA) & 1) ^ 1, kDevTimeoutPipeline);
@@ -279,15 +291,17 @@ PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInf
     (void)K; (void)G;
     const int n_tiles = (N + kPfRows - 1) / kPfRows;
     if (config < 1 || config > 4) {
-        // Wave-quantised cost of the MMA work; below TOK ~ 96 the per-k-step
-        // dequant (fixed 128 x 64 weights) rather than the MMA sets the pace.
+        // Wave-quantised cost of a tile.  A k-step always dequantises a fixed 128 x 64
+        // weight tile, which on B200 costs about as much as the MMA of a 200-token tile
+        // (measured: a 128-token tile takes ~0.79x the time of a 256-token one), so below
+        // that the dequant, not the MMA, sets the pace.
         double best = 1e300;
         config = 3;
         for (int c = 4; c >= 1; --c) {
             const int tok = pf_tok_of_config(c);
             const double tiles = (double)n_tiles * ((M + tok - 1) / tok);
             const double waves = std::ceil(tiles / dev.num_sms);
-            const double cost = waves * std::max(tok, 96);
+            const double cost = waves * std::max(tok, 200);
             if (cost < best - 1e-9) { best = cost; config = c; }
         }
     }
