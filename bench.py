@@ -280,7 +280,7 @@ def run_ours(args):
                 u["layer"].local(u["x"], out=u["y_local"])
                 u["layer"].gather(u["y_local"], out=u["y"])
 
-    # kernels of ours per step: each GEMM is decode_kernel (+ decode_fixup_kernel when a column
+    # kernels of ours per step: each GEMM is decode_kernel (+ decode_combine_kernel when a column
     # group is split across CTAs), as the route query reports
     launches_per_step = 0
     for u in units:
