@@ -68,6 +68,11 @@ typedef enum w4a16_out_dtype {
     W4A16_OUT_F32 = 1                /* y is fp32 [M, N] (row-parallel partial sums) */
 } w4a16_out_dtype;
 
+typedef enum w4a16_w_dtype {
+    W4A16_W_F32 = 0,                 /* unquantised weights are fp32 [N, K] */
+    W4A16_W_F16 = 1                  /* unquantised weights are fp16 [N, K] */
+} w4a16_w_dtype;
+
 typedef struct w4a16_route {
     int32_t kernel;     /* 0 = decode (M <= 16 weight-streaming GEMV), 1 = prefill (tcgen05) */
     int32_t config;     /* prefill tile config 1..4 (token tile 32/64/128/256); 0 for decode */
@@ -134,6 +139,28 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
  * dequantize_w4 (tests/quant.py:77-80).  Debug / verification entry. */
 w4a16_status w4a16_dequant(const int32_t* Wp, const void* scales, void* out,
                            int64_t N, int64_t K, int64_t groups, void* stream);
+
+/* Load-time weight preparation on the GPU (row (f): the steps before the GEMM).  All
+ * pointers are device pointers, 16-byte aligned; N % 16 == 0, K % 64 == 0.  Inputs are
+ * expected finite.  Return after enqueueing on `stream`. */
+
+/* q: uint8 codes [N, K] (values 0..15; only the low 4 bits are read) -> Wp int32 [N*K/8]
+ * in the kernel word order.  Replaces the reference's CPU/torch pack_int4
+ * (tests/quant.py:34-48), bit for bit. */
+w4a16_status w4a16_pack(const uint8_t* q, int32_t* Wp, int64_t N, int64_t K, void* stream);
+
+/* W [N, K] (fp32 or fp16, w_dtype) -> q uint8 codes [N, K] and scales fp16 [K/G, N]:
+ * scale = fp16(max(absmax of the row's G-group / 7, 1e-4)), q = clamp(round-half-even(W /
+ * scale), -8, 7) + 8.  Replaces the reference's quantize_w4 (tests/quant.py:62-74), bit for
+ * bit.  group_size G in {64, 128}. */
+w4a16_status w4a16_quantize(const void* W, int32_t w_dtype, uint8_t* q, void* scales, int64_t N, int64_t K,
+                            int64_t group_size, void* stream);
+
+/* w4a16_quantize followed by w4a16_pack in one pass over W (no code array):
+ * W -> Wp int32 [N*K/8] and scales fp16 [K/G, N].  No counterpart as one call in the
+ * reference (it quantises, then packs). */
+w4a16_status w4a16_quantize_pack(const void* W, int32_t w_dtype, int32_t* Wp, void* scales, int64_t N, int64_t K,
+                                 int64_t group_size, void* stream);
 
 /* Reads the current device's status word, set by a kernel whose bounded wait
  * ran out (0 = none).  Synchronises the device.  reset != 0 clears it. */

@@ -214,6 +214,68 @@ w4a16_status w4a16_dequant(const int32_t* Wp, const void* scales, void* out, int
     return ok();
 }
 
+namespace {
+
+// Shape and pointer checks shared by the load-time format entries.
+w4a16_status check_format(const void* a, const void* b, const void* c, int64_t N, int64_t K, int64_t G) {
+    if (N < 0 || K < 0 || N >= (1LL << 31) || K >= (1LL << 31) || N * K >= (1LL << 40))
+        return fail(W4A16_ERR_DIM_RANGE, "dimensions must fit in int32");
+    if (K % 64 != 0) return fail(W4A16_ERR_K_MULTIPLE, "K must be a multiple of 64");
+    if (N % 16 != 0) return fail(W4A16_ERR_N_MULTIPLE, "N must be a multiple of 16");
+    if (G != 0) {
+        if (G != 64 && G != 128)
+            return fail(W4A16_ERR_GROUP_SIZE, "unsupported group size " + std::to_string(G) + ", supported: 64, 128");
+        if (K % G != 0) return fail(W4A16_ERR_GROUPS, "K must be divisible by the group size");
+    }
+    if (!a || !b || !c) return fail(W4A16_ERR_NULL_POINTER, "pointers must be non-null");
+    if (reinterpret_cast<uintptr_t>(a) % 16 || reinterpret_cast<uintptr_t>(b) % 16 || reinterpret_cast<uintptr_t>(c) % 16)
+        return fail(W4A16_ERR_ALIGNMENT, "pointers must be 16-byte aligned");
+    return ok();
+}
+
+}  // namespace
+
+w4a16_status w4a16_pack(const uint8_t* q, int32_t* Wp, int64_t N, int64_t K, void* stream) {
+    w4a16_status s = check_format(q, Wp, Wp, N, K, 0);
+    if (s != W4A16_OK) return s;
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    if (N == 0 || K == 0) return ok();
+    const cudaError_t err = w4a16::launch_pack(q, Wp, (int)N, (int)K, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_quantize(const void* W, int32_t w_dtype, uint8_t* q, void* scales, int64_t N, int64_t K,
+                            int64_t group_size, void* stream) {
+    if (w_dtype != W4A16_W_F32 && w_dtype != W4A16_W_F16)
+        return fail(W4A16_ERR_OUT_DTYPE, "w_dtype must be 0 (fp32) or 1 (fp16)");
+    w4a16_status s = check_format(W, q, scales, N, K, group_size);
+    if (s != W4A16_OK) return s;
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    if (N == 0 || K == 0) return ok();
+    const cudaError_t err = w4a16::launch_quantize(W, w_dtype == W4A16_W_F16, q, nullptr, scales, (int)N, (int)K,
+                                                   (int)group_size, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_quantize_pack(const void* W, int32_t w_dtype, int32_t* Wp, void* scales, int64_t N, int64_t K,
+                                 int64_t group_size, void* stream) {
+    if (w_dtype != W4A16_W_F32 && w_dtype != W4A16_W_F16)
+        return fail(W4A16_ERR_OUT_DTYPE, "w_dtype must be 0 (fp32) or 1 (fp16)");
+    w4a16_status s = check_format(W, Wp, scales, N, K, group_size);
+    if (s != W4A16_OK) return s;
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    if (N == 0 || K == 0) return ok();
+    const cudaError_t err = w4a16::launch_quantize(W, w_dtype == W4A16_W_F16, nullptr, Wp, scales, (int)N, (int)K,
+                                                   (int)group_size, static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
 w4a16_status w4a16_device_status(int32_t* code, int32_t reset) {
     if (!code) return fail(W4A16_ERR_NULL_POINTER, "code must be non-null");
     int c = 0;

@@ -80,6 +80,14 @@ struct PrefillPlan {
 PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInfo& dev);
 cudaError_t launch_prefill(const GemmArgs& a, const PrefillPlan& p);
 
+// ---------------------------------------------------------------- load-time format kernels
+// codes uint8 [N, K] -> packed words (N % 16 == 0, K % 64 == 0, 16-byte aligned pointers).
+cudaError_t launch_pack(const void* q, void* wp, int N, int K, cudaStream_t stream);
+// W [N, K] fp32 (or fp16 when w_f16) -> scales fp16 [K/G, N] and codes uint8 [N, K] (wp ==
+// nullptr) or packed words (q == nullptr).
+cudaError_t launch_quantize(const void* W, bool w_f16, void* q, void* wp, void* scales, int N, int K, int G,
+                            cudaStream_t stream);
+
 // ---------------------------------------------------------------- debug dequant
 cudaError_t launch_dequant(const void* wp, const void* scales, void* out, int N, int K, int G,
                            cudaStream_t stream);

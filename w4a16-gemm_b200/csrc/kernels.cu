@@ -1,4 +1,4 @@
-// The single device-code translation unit: decode, prefill and dequant kernels,
+// The single device-code translation unit: decode, prefill, dequant and format kernels,
 // the device status word, and the host helpers they need (device properties,
 // shared-memory opt-in, TMA tensor maps).
 #include <cuda.h>
@@ -15,6 +15,7 @@
 #include "decode.cuh"
 #include "prefill.cuh"
 #include "dequant_kernel.cuh"
+#include "format_kernels.cuh"
 
 namespace w4a16 {
 

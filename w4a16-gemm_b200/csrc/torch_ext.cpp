@@ -10,6 +10,7 @@
 
 #include <climits>
 #include <map>
+#include <vector>
 #include <mutex>
 #include <utility>
 
@@ -124,6 +125,36 @@ torch::Tensor w4a16_dequant_py(torch::Tensor Wp, torch::Tensor scales, int64_t K
     return out;
 }
 
+// Load-time format kernels (codes -> packed words; weights -> codes/packed + scales).
+torch::Tensor pack_py(torch::Tensor q) {
+    TORCH_CHECK(q.is_cuda() && q.is_contiguous() && q.dtype() == torch::kUInt8 && q.dim() == 2,
+                "q must be a contiguous CUDA uint8 [N, K] tensor");
+    const at::cuda::CUDAGuard guard(q.device());
+    const int64_t N = q.size(0), K = q.size(1);
+    auto wp = torch::empty({N * K / 8}, q.options().dtype(torch::kInt32));
+    check(w4a16_pack(q.data_ptr<uint8_t>(), wp.data_ptr<int32_t>(), N, K, at::cuda::getCurrentCUDAStream().stream()));
+    return wp;
+}
+
+std::vector<torch::Tensor> quantize_py(torch::Tensor W, int64_t group_size, bool pack) {
+    TORCH_CHECK(W.is_cuda() && W.is_contiguous() && W.dim() == 2, "W must be a contiguous CUDA [N, K] tensor");
+    TORCH_CHECK(W.dtype() == torch::kFloat || W.dtype() == torch::kHalf, "W must be fp32 or fp16");
+    const at::cuda::CUDAGuard guard(W.device());
+    const int64_t N = W.size(0), K = W.size(1);
+    TORCH_CHECK(group_size > 0 && K % group_size == 0, "K must be a multiple of the group size");
+    const int32_t wd = W.dtype() == torch::kHalf ? W4A16_W_F16 : W4A16_W_F32;
+    auto scales = torch::empty({K / group_size, N}, W.options().dtype(torch::kHalf));
+    cudaStream_t st = at::cuda::getCurrentCUDAStream().stream();
+    if (pack) {
+        auto wp = torch::empty({N * K / 8}, W.options().dtype(torch::kInt32));
+        check(w4a16_quantize_pack(W.data_ptr(), wd, wp.data_ptr<int32_t>(), scales.data_ptr(), N, K, group_size, st));
+        return {wp, scales};
+    }
+    auto q = torch::empty({N, K}, W.options().dtype(torch::kUInt8));
+    check(w4a16_quantize(W.data_ptr(), wd, q.data_ptr<uint8_t>(), scales.data_ptr(), N, K, group_size, st));
+    return {q, scales};
+}
+
 pybind11::dict query_route_py(int64_t M, int64_t N, int64_t K, int64_t groups, int64_t variant) {
     w4a16_route r;
     check(w4a16_query_route(M, N, K, groups, clamp_variant(variant), &r));
@@ -164,5 +195,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("groups"), pybind11::arg("variant") = -1);
     m.def("device_status", &device_status_py, "device status word set by timed-out kernel waits",
           pybind11::arg("reset") = false);
+    m.def("pack", &pack_py, "uint8 codes [N, K] -> packed int32 words (GPU)", pybind11::arg("q"));
+    m.def("quantize", &quantize_py, "fp32/fp16 W [N, K] -> (codes or packed words, fp16 scales [K/G, N]) (GPU)",
+          pybind11::arg("W"), pybind11::arg("group_size"), pybind11::arg("pack") = false);
     m.attr("ABI_VERSION") = w4a16_abi_version();
 }

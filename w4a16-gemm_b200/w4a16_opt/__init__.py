@@ -29,7 +29,7 @@ except ImportError as exc:  # pragma: no cover - exercised only when unbuilt
         "run `python w4a16-gemm_b200/build.py`"
     ) from exc
 
-from .format import dequantize_w4, pack_int4, quantize_w4, unpack_int4  # noqa: E402
+from .format import dequantize_w4, pack_int4, quantize_pack, quantize_w4, unpack_int4  # noqa: E402
 
 LIBRARY_PATH = os.path.join(_HERE, "libw4a16.so")
 ABI_VERSION = _C.ABI_VERSION
@@ -84,6 +84,6 @@ def device_status(reset: bool = False) -> int:
 __all__ = [
     "w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status",
     "workspace_bytes", "make_workspace",
-    "pack_int4", "unpack_int4", "quantize_w4", "dequantize_w4",
+    "pack_int4", "unpack_int4", "quantize_w4", "quantize_pack", "dequantize_w4",
     "LIBRARY_PATH", "ABI_VERSION", "PREFILL_VARIANTS",
 ]

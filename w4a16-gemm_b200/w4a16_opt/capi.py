@@ -42,6 +42,9 @@ EXPORTS = {
     "w4a16_gemm_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "w4a16_query_route": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(Route)]),
     "w4a16_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "w4a16_pack": (_i32, [_vp, _vp, _i64, _i64, _vp]),
+    "w4a16_quantize": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "w4a16_quantize_pack": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _vp]),
     "w4a16_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
     "w4a16_status_string": (ctypes.c_char_p, [_i32]),
     "w4a16_last_error": (ctypes.c_char_p, []),

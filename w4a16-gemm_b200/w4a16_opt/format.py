@@ -9,13 +9,22 @@ packed so that each lane's 32-bit word is an mma.m16n8k16 A fragment: word
 4i..4i+3), the code at n = 16*nb + g + 8*((i&3)&1), k = 64*kc + 16*s + 2t +
 8*((i&3)>>1) + (i>>2), with g = lane // 4, t = lane % 4.
 
-These functions produce operands for the GEMM; they are not on its hot path.
+These functions produce operands for the GEMM; they are not on its hot path.  On
+CUDA tensors, ``pack_int4``, ``quantize_w4`` and ``quantize_pack`` run the library's
+format kernels (w4a16_pack / w4a16_quantize / w4a16_quantize_pack); on CPU tensors
+(and non-fp32/fp16 weights) they run the torch restatement below, with the same
+results bit for bit.
 """
 from __future__ import annotations
 
 import torch
 
-__all__ = ["pack_int4", "unpack_int4", "quantize_w4", "dequantize_w4"]
+__all__ = ["pack_int4", "unpack_int4", "quantize_w4", "quantize_pack", "dequantize_w4"]
+
+
+def _ext():
+    from . import _C
+    return _C
 
 
 def _lane_tables(device):
@@ -35,6 +44,8 @@ def pack_int4(q: torch.Tensor) -> torch.Tensor:
     N, K = q.shape
     if N % 16 or K % 64:
         raise ValueError("N must be a multiple of 16 and K of 64")
+    if q.is_cuda and q.dtype == torch.uint8:
+        return _ext().pack(q.contiguous())
     NB, KC = N // 16, K // 64
     n_in, k_in = _lane_tables(q.device)
     # tiles[nb, kc, s, 16 n, 16 k]
@@ -65,10 +76,22 @@ def quantize_w4(W: torch.Tensor, group_size: int):
     G = group_size
     if K % G:
         raise ValueError("K must be a multiple of the group size")
+    if W.is_cuda and W.dtype in (torch.float32, torch.float16) and G in (64, 128) and N % 16 == 0 and K % 64 == 0:
+        q, s = _ext().quantize(W.contiguous(), G, False)
+        return q, s
     grouped = W.float().reshape(N, K // G, G)
     s = (grouped.abs().amax(-1, keepdim=True) / 7).clamp_min(1e-4).half().float()
     q = (torch.round(grouped / s).clamp(-8, 7) + 8).to(torch.uint8).reshape(N, K)
     return q, s.squeeze(-1).t().contiguous().half()
+
+
+def quantize_pack(W: torch.Tensor, group_size: int):
+    """quantize_w4 then pack_int4 in one pass: returns (Wp int32 [N*K/8], scales fp16 [K/G, N])."""
+    if W.is_cuda and W.dtype in (torch.float32, torch.float16):
+        Wp, s = _ext().quantize(W.contiguous(), group_size, True)
+        return Wp, s
+    q, s = quantize_w4(W, group_size)
+    return pack_int4(q), s
 
 
 def dequantize_w4(q: torch.Tensor, scales: torch.Tensor, group_size: int) -> torch.Tensor:
