@@ -21,7 +21,9 @@
 //   warps 2..   dequant (kPfDqPhases groups of 8): warp w owns n16 block
 //               2*(w%4) + ((w-2)/4 & 1) of the tile, i.e. TMEM lanes inside its own
 //               lane quarter, for the k-steps of its group ((w-2)/8)
-//   last 4      epilogue: tcgen05.ld of the accumulator, fp16/fp32 stores
+//   last 16     epilogue: four warps per lane quarter, each tcgen05.ld's a quarter of
+//               the tile's token columns; fp16 results are held in registers and the
+//               accumulator is released before the global stores
 //
 // K is walked in one sequential order for every tile shape, so all prefill
 // configs (TOK = 32/64/128/256) give bit-identical results and a row's output
@@ -47,8 +49,14 @@ namespace w4a16 {
 // it with it % kPfDqPhases == p, so consecutive k-steps are dequantised concurrently.
 constexpr int kPfDqPhases = W4A16_PF_DQ_PHASES;
 constexpr int kPfDqWarps = 8 * kPfDqPhases;
-constexpr int kPfEpiWarp0 = 2 + kPfDqWarps;   // first of the 4 epilogue warps
-constexpr int kPfThreads = (kPfEpiWarp0 + 4) * 32;
+constexpr int kPfEpiWarp0 = 2 + kPfDqWarps;   // first epilogue warp
+// Epilogue warps: four per TMEM lane quarter, each draining a quarter of a tile's token
+// columns into registers, so the accumulator is free for the next tile's MMAs early.
+#ifndef W4A16_PF_EPI_WARPS
+#define W4A16_PF_EPI_WARPS 16
+#endif
+constexpr int kPfEpiWarps = W4A16_PF_EPI_WARPS;
+constexpr int kPfThreads = (kPfEpiWarp0 + kPfEpiWarps) * 32;
 constexpr int kPfRows = 128;                 // output channels per tile (UMMA M)
 constexpr int kPfWBytes = 8 * 512;           // packed words: 8 n16 blocks x one 64-k chunk
 constexpr int kPfSBytes = kPfRows * 2;       // one fp16 scale row slice
@@ -124,7 +132,7 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
         for (int b = 0; b < NACC; ++b) {
             mbar_init(accfull(b), 1);
-            mbar_init(accempty(b), 4 * 32);
+            mbar_init(accempty(b), kPfEpiWarps * 32);
         }
         mbar_init(done_bar, 1);
         fence_mbar_init();
@@ -236,7 +244,11 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
         }
     } else {
         // ------------------------------------------------------------ epilogue
-        const int q = warp & 3;
+        // warp (quarter q, part h) owns output channels 32q..32q+31 of the tile (TMEM lanes)
+        // and token columns [h*CW, (h+1)*CW) of the accumulator
+        constexpr int CW = TOK / (kPfEpiWarps / 4);
+        constexpr int EC = CW < 16 ? CW : 16;                 // columns per tcgen05.ld
+        const int q = warp & 3, h = (warp - kPfEpiWarp0) >> 2;
         const uint32_t lane_field = (uint32_t)(32 * q) << 16;
         int tc = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x, ++tc) {
@@ -245,29 +257,53 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
             if (!__all_sync(0xffffffffu, mbar_wait(accfull(b), (tc / NACC) & 1, kDevTimeoutPipeline))) break;
             tc_fence_after();
             const int n = tn * kPfRows + 32 * q + lane;
-            const int tok0 = tt * TOK;
+            const int tok0 = tt * TOK + h * CW;
+            const uint32_t tcol = tmem + lane_field + (uint32_t)(b * TOK + h * CW);
+            if (OUT_F32) {
 #pragma unroll 1
-            for (int c0 = 0; c0 < TOK && tok0 + c0 < M; c0 += 32) {
-                uint32_t r[32];
-                tmem_ld_32x32b_x32(tmem + lane_field + (uint32_t)(b * TOK + c0), r);
-                tc_wait_ld();
-                if (n < N) {
-                    const int jmax = min(32, M - (tok0 + c0));
-                    if (OUT_F32) {
+                for (int c0 = 0; c0 < CW && tok0 + c0 < M; c0 += EC) {
+                    uint32_t r[EC];
+                    tmem_ld_cols<EC>(tcol + (uint32_t)c0, r);
+                    tc_wait_ld();
+                    if (n < N) {
+                        const int jmax = min(EC, M - (tok0 + c0));
                         float* y = static_cast<float*>(yv) + (size_t)(tok0 + c0) * N + n;
 #pragma unroll
-                        for (int j = 0; j < 32; ++j)
+                        for (int j = 0; j < EC; ++j)
                             if (j < jmax) y[(size_t)j * N] = __uint_as_float(r[j]);
-                    } else {
-                        __half* y = static_cast<__half*>(yv) + (size_t)(tok0 + c0) * N + n;
-#pragma unroll
-                        for (int j = 0; j < 32; ++j)
-                            if (j < jmax) y[(size_t)j * N] = __float2half_rn(__uint_as_float(r[j]));
                     }
                 }
+                tc_fence_before();
+                mbar_arrive(accempty(b));
+            } else {
+                // all of this warp's columns into registers as fp16 pairs, release the
+                // accumulator, then store
+                uint32_t hv[CW / 2];
+#pragma unroll
+                for (int c0 = 0; c0 < CW; c0 += EC) {
+                    uint32_t r[EC];
+                    tmem_ld_cols<EC>(tcol + (uint32_t)c0, r);
+                    tc_wait_ld();
+#pragma unroll
+                    for (int j = 0; j < EC; j += 2) {
+                        const __half2 v = __floats2half2_rn(__uint_as_float(r[j]), __uint_as_float(r[j + 1]));
+                        hv[(c0 + j) / 2] = *reinterpret_cast<const uint32_t*>(&v);
+                    }
+                }
+                tc_fence_before();
+                mbar_arrive(accempty(b));
+                if (n < N) {
+                    const int jmax = min(CW, M - tok0);
+                    __half* y = static_cast<__half*>(yv) + (size_t)tok0 * N + n;
+#pragma unroll
+                    for (int j = 0; j < CW; ++j)
+                        if (j < jmax) {
+                            const uint32_t w = hv[j / 2];
+                            const uint16_t bits = (j & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFF);
+                            y[(size_t)j * N] = *reinterpret_cast<const __half*>(&bits);
+                        }
+                }
             }
-            tc_fence_before();
-            mbar_arrive(accempty(b));
         }
     }
 

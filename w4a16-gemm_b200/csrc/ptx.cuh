@@ -351,6 +351,31 @@ __device__ __forceinline__ void tmem_st_16x128b_x8(uint32_t taddr, const uint32_
         : "memory");
 }
 
+// 32 lanes x 16 columns: thread L gets lane base + L, columns c..c+15.
+__device__ __forceinline__ void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t (&r)[16]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+        : "r"(taddr) : "memory");
+}
+
+// 32 lanes x 8 columns: thread L gets lane base + L, columns c..c+7.
+__device__ __forceinline__ void tmem_ld_32x32b_x8(uint32_t taddr, uint32_t (&r)[8]) {
+    asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+                 : "r"(taddr) : "memory");
+}
+
+// tcgen05.ld of C (8 or 16) consecutive accumulator columns of this warp's 32 lanes.
+template <int C>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[C]) {
+    static_assert(C == 8 || C == 16, "columns per load");
+    if constexpr (C == 16) tmem_ld_32x32b_x16(taddr, r);
+    else tmem_ld_32x32b_x8(taddr, r);
+}
+
 // 32 lanes x 32 columns: thread L gets lane base + L, columns c..c+31.
 __device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
     asm volatile(
