@@ -35,6 +35,9 @@
 #include <stdint.h>
 
 #include <algorithm>
+#include <map>
+#include <mutex>
+#include <tuple>
 
 #include "dequant.cuh"
 #include "internal.h"
@@ -84,6 +87,7 @@ struct DcPartition {
     int total;     // groups * kc
     int ctas;      // CTAs (<= total)
     bool valid;    // total fits 32 bits
+    bool split;    // some group is split across CTAs (a CTA boundary inside a group)
     __host__ __device__ int c0(int c) const { return (int)(((long long)c * total) / ctas); }
     // First / last CTA whose range intersects group g (closed forms of "largest c with
     // c0(c) <= g*kc" and "largest c with c0(c) < (g+1)*kc"; one division each).
@@ -101,7 +105,7 @@ struct DcPartition {
     __host__ __device__ int slot(int c, int g) const { return 2 * c + (g == c0(c) / kc ? 0 : 1); }
 };
 
-__host__ __device__ inline DcPartition dc_partition(int N, int K, int num_sms) {
+inline DcPartition dc_cut(int N, int K, int num_sms) {
     DcPartition p;
     p.groups = (N / 16 + kDcBlocks - 1) / kDcBlocks;
     p.kc = K / 64;
@@ -111,21 +115,29 @@ __host__ __device__ inline DcPartition dc_partition(int N, int K, int num_sms) {
     const int cap = p.total / kDcMinUnits > 0 ? p.total / kDcMinUnits : 1;
     p.ctas = num_sms < cap ? num_sms : cap;
     if (p.ctas > kDcMaxCTAs) p.ctas = kDcMaxCTAs;
+    p.split = false;
+    for (int c = 1; c < p.ctas && !p.split; ++c) p.split = p.c0(c) % p.kc != 0;
     return p;
 }
 
-// True if some group is split across CTAs (a CTA boundary inside a group).
-__host__ __device__ inline bool dc_has_split(const DcPartition& p) {
-    for (int c = 1; c < p.ctas; ++c)
-        if (p.c0(c) % p.kc != 0) return true;
-    return false;
+// The partition of a shape, computed once per (N, K, #SMs): a GEMM call consults it a few
+// times on the host, and finding whether a group is split walks every CTA boundary.
+inline DcPartition dc_partition(int N, int K, int num_sms) {
+    static std::mutex mu;
+    static std::map<std::tuple<int, int, int>, DcPartition> cache;
+    const auto key = std::make_tuple(N, K, num_sms);
+    std::lock_guard<std::mutex> lk(mu);
+    const auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+    if (cache.size() >= 4096) cache.clear();
+    return cache[key] = dc_cut(N, K, num_sms);
 }
 
 // Workspace: 2 fp32 partial slots per CTA (a CTA's range splits at most its first
 // and its last group), only when some group is split.  Always fully written before
 // it is read; no initial contents are assumed.
-__host__ __device__ inline size_t dc_workspace_bytes(const DcPartition& p) {
-    return dc_has_split(p) ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
+inline size_t dc_workspace_bytes(const DcPartition& p) {
+    return p.split ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
 }
 
 // Walks a CTA's chunk range [pos, end) in steps of <= kDcStep chunks that never
@@ -408,7 +420,7 @@ DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
     p.stages = DcCfg<8>::ST;
     p.smem = p.mt == 1 ? DcCfg<8>::SMEM : DcCfg<16>::SMEM;
     p.workspace = dc_workspace_bytes(part);
-    p.launches = dc_has_split(part) ? 2 : 1;
+    p.launches = part.split ? 2 : 1;
     p.valid = part.valid;
     return p;
 }
@@ -448,7 +460,7 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     cfg.attrs = &attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
     err = cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, box_chunks, part, partials);
-    if (err != cudaSuccess || !dc_has_split(part)) return err;
+    if (err != cudaSuccess || !part.split) return err;
     // combine split groups; always launched programmatically dependent on decode_kernel
     cudaLaunchConfig_t fc = {};
     fc.gridDim = dim3(part.groups, a.M, 1);
