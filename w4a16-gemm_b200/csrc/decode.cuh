@@ -300,7 +300,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                     s_hi[bb][j] = j < nk ? bcast_half(hi) : 0u;
                 }
             const uint32_t wb = sb + w_lane;
-            constexpr int JB = MT == 1 ? 4 : 1;                // chunks whose operands are loaded together
+            constexpr int JB = MT == 1 ? 4 : 2;                // chunks whose operands are loaded together
 #pragma unroll
             for (int jb = 0; jb < kDcStep; jb += JB) {
                 uint4 wv[JB][BPW];
