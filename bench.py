@@ -227,6 +227,9 @@ def run_ours(args):
     world, rank, local = dist_env()
     torch.cuda.set_device(local)
     if world > 1:
+        # rank 0's stdout carries exactly one JSON line: NCCL's own messages (its version
+        # banner, debug output) go to stderr unless the caller chose a destination
+        os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
         import datetime
 
         import torch.distributed as dist
