@@ -36,8 +36,6 @@ cudaError_t device_info(DeviceInfo* out);
 // per (kernel, device) (thread-safe).
 cudaError_t ensure_max_dynamic_smem(const void* func);
 
-// Allow clusters of more than 8 CTAs for a kernel (once per kernel and device).
-cudaError_t ensure_nonportable_cluster(const void* func);
 
 // Read (and optionally clear) the device status word that bounded waits set on
 // timeout.  Synchronises with the device.

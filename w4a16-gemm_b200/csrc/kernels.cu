@@ -58,19 +58,6 @@ cudaError_t ensure_max_dynamic_smem(const void* func) {
     return err;
 }
 
-cudaError_t ensure_nonportable_cluster(const void* func) {
-    static std::mutex mu;
-    static std::set<std::pair<const void*, int>> done;
-    DeviceInfo d;
-    cudaError_t err = device_info(&d);
-    if (err != cudaSuccess) return err;
-    std::lock_guard<std::mutex> lk(mu);
-    if (done.count({func, d.device})) return cudaSuccess;
-    err = cudaFuncSetAttribute(func, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
-    if (err == cudaSuccess) done.insert({func, d.device});
-    return err;
-}
-
 cudaError_t read_device_status(int* code, bool reset) {
     cudaError_t err = cudaDeviceSynchronize();
     if (err != cudaSuccess) return err;

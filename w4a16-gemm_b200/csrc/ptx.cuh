@@ -1,6 +1,6 @@
-// Thin inline-PTX wrappers for sm_100a: mbarriers, bulk / tensor copies (TMA),
-// cluster shared memory, tcgen05 (TMEM alloc, MMA, ld/st), programmatic
-// dependent launch, and a bounded-wait policy.
+// Thin inline-PTX wrappers for sm_100a: mbarriers, tensor copies (TMA),
+// tcgen05 (TMEM alloc, MMA, ld/st), programmatic dependent launch, and a
+// bounded-wait policy.
 //
 // Every spin-wait in this library is bounded by wall time (globaltimer).  A
 // wait that runs out records a code in the per-device status word
@@ -22,7 +22,6 @@ enum DeviceError : int {
     kDevOk = 0,
     kDevTimeoutWeights = 1,      // decode: weight ring barrier never completed
     kDevTimeoutActivations = 2,  // decode: activation / scale barrier never completed
-    kDevTimeoutCluster = 3,      // decode: cluster split-K barrier never completed
     kDevTimeoutPipeline = 4,     // prefill: a producer/consumer barrier never completed
     kDevTimeoutDrain = 5,        // error path: in-flight copies did not land in time
 };
@@ -73,26 +72,11 @@ __device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
     asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
 }
 
-// Arrive on an mbarrier of another CTA of the cluster (address from mapa).
-__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_bar) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" :: "r"(cluster_bar) : "memory");
-}
-
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
         "{\n\t.reg .pred p;\n\t"
         "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
         "selp.u32 %0, 1, 0, p;\n\t}"
         : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
     return ok != 0;
@@ -139,94 +123,11 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int cod
     }
 }
 
-__device__ __forceinline__ bool mbar_wait_cluster(uint32_t bar, uint32_t parity, int code) {
-    if (mbar_try_wait_cluster(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-        for (int i = 0; i < 64; ++i)
-            if (mbar_try_wait_cluster(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            record_device_error(code);
-            return false;
-        }
-    }
-}
-
-// ------------------------------------------------------------------ cluster
-__device__ __forceinline__ uint32_t cluster_ctarank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// Map a CTA-local shared address to the same offset in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
-    return r;
-}
-
-__device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
-    float v;
-    asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
-    return v;
-}
-
-__device__ __forceinline__ void cluster_arrive_release() {
-    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_wait_acquire() {
-    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-__device__ __forceinline__ void cluster_sync() {
-    cluster_arrive_release();
-    cluster_wait_acquire();
-}
-
-// ------------------------------------------------------------------ copies
-// 1-D bulk copy global -> own shared memory, completion signalled on `bar`.
-// Requires 16-byte aligned addresses and a size that is a multiple of 16.
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-        :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
-}
-
-// Same, with an L2 eviction-priority hint (createpolicy result).
-__device__ __forceinline__ void bulk_g2s_hint(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar,
-                                              uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;"
-        :: "r"(dst), "l"(src), "r"(bytes), "r"(bar), "l"(policy) : "memory");
-}
-
-__device__ __forceinline__ uint64_t policy_evict_first() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-
-__device__ __forceinline__ uint64_t policy_evict_last() {
-    uint64_t p;
-    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
-    return p;
-}
-
 // Tiled tensor copies (TMA), no multicast.
 __device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, int c0, int c1, uint32_t bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
         :: "r"(dst), "l"(tmap), "r"(c0), "r"(c1), "r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d_hint(uint32_t dst, const void* tmap, int c0, int c1, uint32_t bar,
-                                                 uint64_t policy) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-        " [%0], [%1, {%2, %3}], [%4], %5;"
-        :: "r"(dst), "l"(tmap), "r"(c0), "r"(c1), "r"(bar), "l"(policy) : "memory");
 }
 
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int c0, int c1, int c2, uint32_t bar) {
@@ -235,24 +136,8 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, int 
         :: "r"(dst), "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(bar) : "memory");
 }
 
-// Pull a line into L2 (no register result): hides DRAM latency of a later load.
-__device__ __forceinline__ void prefetch_l2(const void* p) {
-    asm volatile("prefetch.global.L2::evict_last [%0];" :: "l"(p));
-}
-
 __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
-}
-
-// 16-byte async copy global -> shared (L2 only), and an mbarrier arrival that
-// fires once all of this thread's earlier cp.async copies have landed (the
-// barrier's expected count must include these arrivals: .noinc).
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(dst), "l"(src) : "memory");
-}
-
-__device__ __forceinline__ void cp_async_arrive_noinc(uint32_t bar) {
-    asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" :: "r"(bar) : "memory");
 }
 
 // ------------------------------------------------------------------ PDL
@@ -374,19 +259,6 @@ __device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&r)[C]) {
     static_assert(C == 8 || C == 16, "columns per load");
     if constexpr (C == 16) tmem_ld_32x32b_x16(taddr, r);
     else tmem_ld_32x32b_x8(taddr, r);
-}
-
-// 32 lanes x 32 columns: thread L gets lane base + L, columns c..c+31.
-__device__ __forceinline__ void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
-    asm volatile(
-        "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
-        "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
-        "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
-        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
-          "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]),
-          "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]),
-          "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-        : "r"(taddr) : "memory");
 }
 
 }  // namespace w4a16
