@@ -22,6 +22,14 @@
  * workspace serves any number of calls, of any shapes, issued in stream order.
  * Calls that may run concurrently need separate workspaces.
  *
+ * Stream order: the decode kernel is launched with programmatic dependent launch
+ * and starts fetching Wp and scales before the kernel launched just before it on
+ * the stream is known to have finished (x, y and the workspace are touched only
+ * after that kernel's writes are visible).  So Wp and scales must not be written
+ * by the kernel launched immediately before the GEMM: write them with a copy, with
+ * this library's format entry points (which end with an empty kernel for this
+ * reason), or put any other kernel launch or a synchronisation in between.
+ *
  * This header replaces the reference's torch-typed entry point
  *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)
  * (akshay919191/W4A16-GEMM src/vectorized/kernel.cu:218, bound as
@@ -140,9 +148,10 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
 w4a16_status w4a16_dequant(const int32_t* Wp, const void* scales, void* out,
                            int64_t N, int64_t K, int64_t groups, void* stream);
 
-/* Load-time weight preparation on the GPU (row (f): the steps before the GEMM).  All
+/* Load-time weight preparation on the GPU (the steps before the GEMM).  All
  * pointers are device pointers, 16-byte aligned; N % 16 == 0, K % 64 == 0.  Inputs are
- * expected finite.  Return after enqueueing on `stream`. */
+ * expected finite.  Return after enqueueing on `stream`; each enqueues its kernel and
+ * then an empty kernel, so a GEMM launched right after reads the finished weights. */
 
 /* q: uint8 codes [N, K] (values 0..15; only the low 4 bits are read) -> Wp int32 [N*K/8]
  * in the kernel word order.  Replaces the reference's CPU/torch pack_int4

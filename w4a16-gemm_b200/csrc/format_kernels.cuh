@@ -121,11 +121,25 @@ __global__ void __launch_bounds__(kFmtThreads) quantize_kernel(const T* __restri
     }
 }
 
+// The GEMM's decode kernel is launched with programmatic dependent launch and fetches
+// packed words and scales before griddepcontrol.wait, so it may start while the kernel
+// launched just before it is still finishing.  An empty kernel, launched without that
+// attribute, after every format kernel makes the weights complete before a GEMM that
+// follows can start.
+__global__ void format_fence_kernel() {}
+
+static cudaError_t fence_after(cudaStream_t stream) {
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    format_fence_kernel<<<1, 32, 0, stream>>>();
+    return cudaGetLastError();
+}
+
 // ------------------------------------------------------------------ host side
 cudaError_t launch_pack(const void* q, void* wp, int N, int K, cudaStream_t stream) {
     pack_kernel<<<dim3(K / 64, N / 16), kFmtThreads, 0, stream>>>(static_cast<const uint8_t*>(q),
                                                                     static_cast<uint32_t*>(wp), N, K);
-    return cudaGetLastError();
+    return fence_after(stream);
 }
 
 template <typename T, bool PACK>
@@ -139,7 +153,7 @@ static cudaError_t launch_quantize_t(const void* W, void* q, void* wp, void* sca
     else
         quantize_kernel<T, 128, PACK><<<grid, kFmtThreads, 0, stream>>>(w, static_cast<uint8_t*>(q),
             static_cast<uint32_t*>(wp), static_cast<__half*>(scales), N, K);
-    return cudaGetLastError();
+    return fence_after(stream);
 }
 
 cudaError_t launch_quantize(const void* W, bool w_f16, void* q, void* wp, void* scales, int N, int K, int G,
