@@ -28,7 +28,9 @@
  * after that kernel's writes are visible).  So Wp and scales must not be written
  * by the kernel launched immediately before the GEMM: write them with a copy, with
  * this library's format entry points (which end with an empty kernel for this
- * reason), or put any other kernel launch or a synchronisation in between.
+ * reason), or put any other kernel launch or a synchronisation in between.  The
+ * environment variable W4A16_PDL=0 (read once per process) launches every kernel
+ * in plain stream order instead, which lifts this rule and gives up the overlap.
  *
  * This header replaces the reference's torch-typed entry point
  *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)

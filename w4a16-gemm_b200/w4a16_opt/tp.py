@@ -32,6 +32,14 @@ def _default_gemm_out(Wp, x, scales, y, workspace=None):
     return w4a16_gemm_out(Wp, x, scales, y, workspace=workspace)
 
 
+def _settle(*tensors: torch.Tensor) -> None:
+    """Wait for the copies that made CUDA shards.  The GEMM reads weights before its
+    dependent-launch wait, so they must not come from the kernel launched just before it."""
+    for t in tensors:
+        if t.is_cuda:
+            torch.cuda.current_stream(t.device).synchronize()
+
+
 def shard_columns(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int, world: int):
     """(Wp_r, scales_r) for rank r of a column-parallel split of N."""
     NB, KC = N // 16, K // 64
@@ -40,6 +48,7 @@ def shard_columns(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: 
     nb = NB // world
     Wp_r = Wp.view(NB, KC, 32, 4)[rank * nb:(rank + 1) * nb].contiguous().view(-1)
     s_r = scales[:, rank * nb * 16:(rank + 1) * nb * 16].contiguous()
+    _settle(Wp_r, s_r)
     return Wp_r, s_r
 
 
@@ -53,6 +62,7 @@ def shard_rows(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int
     Wp_r = Wp.view(NB, KC, 32, 4)[:, rank * kc:(rank + 1) * kc].contiguous().view(-1)
     gpr = (K // world) // G
     s_r = scales[rank * gpr:(rank + 1) * gpr].contiguous()
+    _settle(Wp_r, s_r)
     return Wp_r, s_r
 
 
