@@ -39,24 +39,16 @@
 #include <mutex>
 #include <tuple>
 
+#include "decode_partition.h"
 #include "dequant.cuh"
 #include "internal.h"
 #include "ptx.cuh"
 
 namespace w4a16 {
 
-constexpr int kDcBlocks = 16;                             // n16 blocks per group
 constexpr int kDcBPW = 2;                                 // n16 blocks per consumer warp
 constexpr int kDcWarps = kDcBlocks / kDcBPW;              // consumer warps; warp w owns blocks 2w, 2w+1
 constexpr int kDcThreads = (kDcWarps + 1) * 32;           // + the producer warp
-constexpr int kDcCols = kDcBlocks * 16;                   // output columns per group
-constexpr int kDcStep = 4;                                // 64-wide K chunks per step
-constexpr int kDcSlotFloats = 16 * kDcCols;               // one partial: 16 tokens x 256 columns
-constexpr int kDcMaxCTAs = 1024;
-// Fewest (group, chunk) units a CTA gets: a small GEMM runs on fewer CTAs rather than
-// splitting each column group over dozens of them (its copies are all in flight at once
-// either way, and the combine reads fewer partials).
-constexpr int kDcMinUnits = 4;
 // Ring stages of packed words and scales issued before griddepcontrol.wait.  More is not
 // better: a deep early burst from the next GEMM delays the previous GEMM's combine
 // kernel (measured on the decode sweep: 2 stages 2073 GB/s, all 5 stages 1934 GB/s).
@@ -80,46 +72,6 @@ struct DcCfg {
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
-// Static stream-K partition over (group, chunk) pairs, identical on host and device.
-struct DcPartition {
-    int groups;    // 256-column groups
-    int kc;        // 64-wide K chunks per group (K / 64)
-    int total;     // groups * kc
-    int ctas;      // CTAs (<= total)
-    bool valid;    // total fits 32 bits
-    bool split;    // some group is split across CTAs (a CTA boundary inside a group)
-    __host__ __device__ int c0(int c) const { return (int)(((long long)c * total) / ctas); }
-    // First / last CTA whose range intersects group g (closed forms of "largest c with
-    // c0(c) <= g*kc" and "largest c with c0(c) < (g+1)*kc"; one division each).
-    __host__ __device__ int first_cta(int g) const {
-        const unsigned long long lo = (unsigned long long)g * kc;
-        const int c = (int)(((lo + 1) * (unsigned)ctas - 1) / (unsigned)total);
-        return c < ctas - 1 ? c : ctas - 1;
-    }
-    __host__ __device__ int last_cta(int g) const {
-        const unsigned long long hi = (unsigned long long)(g + 1) * kc;
-        const int c = (int)((hi * (unsigned)ctas - 1) / (unsigned)total);
-        return c < ctas - 1 ? c : ctas - 1;
-    }
-    // Workspace slot of CTA c's partial of group g (only for split groups).
-    __host__ __device__ int slot(int c, int g) const { return 2 * c + (g == c0(c) / kc ? 0 : 1); }
-};
-
-inline DcPartition dc_cut(int N, int K, int num_sms) {
-    DcPartition p;
-    p.groups = (N / 16 + kDcBlocks - 1) / kDcBlocks;
-    p.kc = K / 64;
-    const long long total = (long long)p.groups * p.kc;
-    p.valid = total > 0 && total < (1ll << 31);
-    p.total = p.valid ? (int)total : 1;
-    const int cap = p.total / kDcMinUnits > 0 ? p.total / kDcMinUnits : 1;
-    p.ctas = num_sms < cap ? num_sms : cap;
-    if (p.ctas > kDcMaxCTAs) p.ctas = kDcMaxCTAs;
-    p.split = false;
-    for (int c = 1; c < p.ctas && !p.split; ++c) p.split = p.c0(c) % p.kc != 0;
-    return p;
-}
-
 // The partition of a shape, computed once per (N, K, #SMs): a GEMM call consults it a few
 // times on the host, and finding whether a group is split walks every CTA boundary.
 inline DcPartition dc_partition(int N, int K, int num_sms) {
@@ -132,29 +84,6 @@ inline DcPartition dc_partition(int N, int K, int num_sms) {
     if (cache.size() >= 4096) cache.clear();
     return cache[key] = dc_cut(N, K, num_sms);
 }
-
-// Workspace: 2 fp32 partial slots per CTA (a CTA's range splits at most its first
-// and its last group), only when some group is split.  Always fully written before
-// it is read; no initial contents are assumed.
-inline size_t dc_workspace_bytes(const DcPartition& p) {
-    return p.split ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
-}
-
-// Walks a CTA's chunk range [pos, end) in steps of <= kDcStep chunks that never
-// cross a group boundary.
-struct DcSteps {
-    int pos, end, g, kc;
-    __device__ void start(int c0, int c1, int KC) { pos = c0; end = c1; g = c0 / KC; kc = c0 - g * KC; }
-    __device__ bool more() const { return pos < end; }
-    __device__ int nk(int KC) const { return min(kDcStep, min(KC - kc, end - pos)); }
-    // Advances past a step of n chunks; true if that step ended this CTA's part of its group.
-    __device__ bool advance(int n, int KC) {
-        pos += n;
-        kc += n;
-        if (kc == KC) { kc = 0; ++g; return true; }
-        return pos == end;
-    }
-};
 
 template <int G, int MP, bool OUT_F32>
 __global__ void __launch_bounds__(kDcThreads, 1)
