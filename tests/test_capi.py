@@ -121,3 +121,31 @@ def test_binding_exports():
     for name in ("w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status"):
         assert callable(getattr(w4a16_opt, name))
     assert w4a16_opt.ABI_VERSION == 2
+
+
+@pytest.mark.skipif(__import__("shutil").which("gcc") is None, reason="needs gcc")
+def test_header_layout_matches_ctypes(tmp_path):
+    """include/w4a16.h compiles as C99, and its struct layout and status codes are the ones
+    the ctypes binding declares (what a cgo / JNI / N-API binding would also rely on)."""
+    import subprocess
+    fields = [name for name, _ in capi.Route._fields_]
+    src = tmp_path / "layout.c"
+    lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "w4a16.h"', "int main(void) {",
+             '    printf("sizeof %zu\\n", sizeof(w4a16_route));']
+    lines += [f'    printf("{f} %zu\\n", offsetof(w4a16_route, {f}));' for f in fields]
+    lines += [f'    printf("{name} %d\\n", (int){name});' for name in capi.STATUS_NAMES.values()]
+    lines += ['    printf("W4A16_OUT_F32 %d\\n", (int)W4A16_OUT_F32);',
+              '    printf("W4A16_ABI_VERSION %d\\n", (int)W4A16_ABI_VERSION);', "    return 0;", "}"]
+    src.write_text("\n".join(lines) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-pedantic", "-I", os.path.join(ROOT, "include"),
+                    str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
+                                                       check=True).stdout.splitlines())
+    assert int(out["sizeof"]) == ctypes.sizeof(capi.Route)
+    for f in fields:
+        assert int(out[f]) == getattr(capi.Route, f).offset, f
+    for code, name in capi.STATUS_NAMES.items():
+        assert int(out[name]) == code, name
+    assert int(out["W4A16_OUT_F32"]) == capi.W4A16_OUT_F32
+    assert int(out["W4A16_ABI_VERSION"]) == capi.load().w4a16_abi_version()
