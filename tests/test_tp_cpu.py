@@ -110,3 +110,57 @@ def test_tp_world2_gloo(M):
         # row split: two fp32 partial sums, one fp16 rounding
         assert float(np.abs(y_row - ref).max()) <= 2e-3 * denom
     assert np.array_equal(out[0][0], out[1][0]) and np.array_equal(out[0][1], out[1][1])
+
+
+def _failing_rank_main(rank, world, port, layer, mode, timeout_s, results):
+    """Rank 1 fails between steps (raises, or stalls and never joins); rank 0 runs the layer."""
+    import datetime
+    import time
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    from w4a16_opt import tp
+    M, N, K, G = 2, 256, 512, 128
+    x, q, s, Wp = _problem(M, N, K, G)
+    cls = tp.ColumnParallelW4A16 if layer == "col" else tp.RowParallelW4A16
+    mod = cls(Wp, s, N, K, gemm_out=_oracle_gemm_out)
+    if rank != 0:
+        if mode == "raise":
+            raise RuntimeError("injected failure on rank 1")
+        time.sleep(timeout_s + 2)             # alive, but never enters the collective
+        os._exit(0)
+    t0 = time.monotonic()
+    try:
+        mod(x) if layer == "col" else mod(mod.x_slice(x))
+        results[rank] = ("completed", time.monotonic() - t0)
+    except Exception as exc:                  # the collective must end with an error, not hang
+        results[rank] = (type(exc).__name__, time.monotonic() - t0)
+    os._exit(0)                               # no teardown collective with a failed peer
+
+
+@pytest.mark.parametrize("layer", ["col", "row"])
+@pytest.mark.parametrize("mode", ["raise", "stall"])
+def test_tp_peer_failure_is_an_error_not_a_hang(layer, mode):
+    """A rank that dies or stalls between steps makes the surviving rank's next collective
+    (all-gather or all-reduce) raise within the process-group timeout."""
+    timeout_s = 3
+    ctx = mp.get_context("spawn")
+    with ctx.Manager() as mgr:
+        results = mgr.dict()
+        port = _free_port()
+        procs = [ctx.Process(target=_failing_rank_main, args=(r, 2, port, layer, mode, timeout_s, results))
+                 for r in range(2)]
+        for p in procs:
+            p.start()
+        for p in procs:
+            p.join(timeout=120)
+        alive = [p for p in procs if p.is_alive()]
+        for p in alive:
+            p.kill()
+        assert not alive, "a rank did not finish"
+        out = dict(results)
+    assert 0 in out, "rank 0 reported nothing"
+    outcome, secs = out[0]
+    assert outcome != "completed", "the collective completed without its peer"
+    assert secs < timeout_s + 30, f"error took {secs:.1f} s"
+    assert procs[1].exitcode == (1 if mode == "raise" else 0)
+    print(f"{layer}/{mode}: rank 0 raised {outcome} after {secs:.1f} s")
