@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <string>
@@ -75,6 +76,29 @@ size_t route_workspace(const Route& r) {
     return r.decode ? r.dp.workspace : 0;
 }
 
+// Route tracing on stderr, read once per process.  W4A16_DEBUG_PREFILL is the reference's
+// switch (src/vectorized/kernel.cu:110-112, 199-201): one line per prefill dispatch with the
+// chosen tile config and pipeline depth.  W4A16_DEBUG_ROUTE adds a line per decode call.
+int debug_level() {
+    static const int level = [] {
+        if (std::getenv("W4A16_DEBUG_ROUTE")) return 2;
+        if (std::getenv("W4A16_DEBUG_PREFILL")) return 1;
+        return 0;
+    }();
+    return level;
+}
+
+void trace_route(const Route& r, int M, int N, int K, int G) {
+    const int level = debug_level();
+    if (level == 0 || (r.decode && level < 2)) return;
+    if (r.decode)
+        std::fprintf(stderr, "w4a16 decode G=%d M=%d N=%d K=%d ctas=%d units=%d stages=%d smem=%zu launches=%d\n", G, M,
+                     N, K, r.dp.ctas, r.dp.units, r.dp.stages, r.dp.smem, r.dp.launches);
+    else
+        std::fprintf(stderr, "w4a16 prefill dispatch G=%d M=%d N=%d K=%d cfg=%d tok=%d grid=%d tiles=%d stages=%d smem=%zu\n",
+                     G, M, N, K, r.pp.config, r.pp.tok, r.pp.grid, r.pp.tiles, r.pp.stages, r.pp.smem);
+}
+
 }  // namespace
 
 extern "C" {
@@ -128,6 +152,7 @@ w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, vo
                                                  std::to_string(need) + " bytes");
         if (reinterpret_cast<uintptr_t>(workspace) % 256) return fail(W4A16_ERR_WORKSPACE, "workspace must be 256-byte aligned");
     }
+    trace_route(r, a.M, a.N, a.K, G);
     cudaError_t err = r.decode ? w4a16::launch_decode(a, r.dp) : w4a16::launch_prefill(a, r.pp);
     if (err == cudaSuccess) err = cudaGetLastError();
     if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
