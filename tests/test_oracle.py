@@ -144,3 +144,71 @@ def test_pack_rejects_bad_shapes():
         oracle.pack_int4(np.zeros((24, 64), np.uint8))
     with pytest.raises(ValueError):
         pack_int4(torch.zeros(16, 96, dtype=torch.uint8))
+
+
+# ---------------------------------------------------------------- properties over random shapes and values
+
+from hypothesis import HealthCheck, assume, given, settings  # noqa: E402
+from hypothesis import strategies as st  # noqa: E402
+
+_shapes = st.tuples(st.integers(1, 6).map(lambda b: 16 * b), st.integers(1, 4).map(lambda c: 64 * c))
+_prop = settings(max_examples=40, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+
+
+@_prop
+@given(shape=_shapes, seed=st.integers(0, 2**31 - 1))
+def test_prop_pack_roundtrip_and_product_equals_oracle(shape, seed):
+    from w4a16_opt import pack_int4, unpack_int4
+    N, K = shape
+    q = np.random.default_rng(seed).integers(0, 16, (N, K), dtype=np.uint8)
+    wp = oracle.pack_int4(q)
+    assert np.array_equal(oracle.unpack_int4(wp, N, K), q)
+    assert np.array_equal(pack_int4(torch.from_numpy(q)).numpy(), wp)
+    assert torch.equal(unpack_int4(torch.from_numpy(wp.view(np.int32)), N, K), torch.from_numpy(q))
+
+
+@_prop
+@given(shape=_shapes, G=st.sampled_from([64, 128]), seed=st.integers(0, 2**31 - 1),
+       scale_exp=st.integers(-12, 3))
+def test_prop_quantize_product_equals_oracle(shape, G, seed, scale_exp):
+    """The product's quantize_w4 (torch) and the oracle's (numpy) agree bit for bit over
+    magnitudes from 2^-12 to 2^3, including the 1e-4 scale floor and exact .5 ties."""
+    from w4a16_opt import quantize_w4
+    N, K = shape
+    assume(K % G == 0)
+    rng = np.random.default_rng(seed)
+    W = (rng.standard_normal((N, K)) * 2.0 ** scale_exp).astype(np.float32)
+    W[0, : min(K, 8)] = np.float32(2.0 ** scale_exp) * np.array([3.5, -3.5, 0.5, -0.5, 7, -7, 0, 2.5],
+                                                                 np.float32)[: min(K, 8)]
+    q_o, s_o = oracle.quantize_w4(W, G)
+    q_p, s_p = quantize_w4(torch.from_numpy(W), G)
+    assert np.array_equal(q_p.numpy(), q_o)
+    assert np.array_equal(s_p.numpy().view(np.uint16), np.asarray(s_o, np.float16).view(np.uint16))
+
+
+@_prop
+@given(shape=_shapes, seed=st.integers(0, 2**31 - 1))
+def test_prop_kernel_word_decode_dequant_equals_reference_dequant(shape, seed):
+    """Dequantising through the kernel's word decode (magic-number form) equals the
+    reference's (q - 8) * scale in fp16 bit for bit, for random codes and scales."""
+    N, K = shape
+    G = 64
+    rng = np.random.default_rng(seed)
+    q = rng.integers(0, 16, (N, K), dtype=np.uint8)
+    s = (rng.random((K // G, N)) * 0.05 + 1e-4).astype(np.float16)
+    wp = oracle.pack_int4(q)
+    ref = oracle.dequantize_w4(q, s, G)
+    words = wp.reshape(N // 16, K // 64, 32, 4)
+    n_idx, k_idx = oracle.fragment_map()
+    for nb in range(N // 16):
+        for kc in range(K // 64):
+            for lane in range(0, 32, 7):
+                for sub in range(4):
+                    pairs = oracle.kernel_word_decode(int(words[nb, kc, lane, sub]))
+                    for p in range(4):
+                        for h in range(2):
+                            i = p + 4 * h
+                            n = nb * 16 + int(n_idx[lane, i])
+                            k = kc * 64 + sub * 16 + int(k_idx[lane, i])
+                            got = np.float16(np.float16(pairs[p][h]) * s[k // G, n])
+                            assert got.view(np.uint16) == ref[n, k].view(np.uint16)
