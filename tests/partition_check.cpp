@@ -8,7 +8,10 @@
 //   * a group inside one CTA is written once to y and no partial is written for it;
 //   * a split group gets one partial from each of CTAs first..last, in distinct slots
 //     below 2 * ctas, at exactly the slots the combine kernel reads;
-//   * the split flag and the workspace size agree with the partials written.
+//   * the split flag and the workspace size agree with the partials written;
+//   * the tensor-copy coordinates the producer issues per step (decode_kernel's
+//     issue_weights and activation copy) start inside the tensors, and every innermost
+//     coordinate is a multiple of 16 bytes (the TMA alignment rule).
 // This is the same role as the reference's numpy emulation of its kernel's data flow
 // (akshay919191/W4A16-GEMM tests/layout.py), for this kernel's work split.
 #include <cstdio>
@@ -55,6 +58,23 @@ static void check_closed_forms(const DcPartition& p, int g, int N, int K, int sm
     CHECK(p.last_cta(g) == l, "last_cta(%d) = %d, expected %d", g, p.last_cta(g), l);
 }
 
+// The copies one step issues, as decode_kernel's producer does: packed words at
+// (0, kc, g * kDcBlocks) of [NB][KC][128] int32, activations at (0, 0, kc) of [KC][M][64]
+// fp16, and per chunk j < nk the scale row ((kc + j) * 64) / G at column g * kDcCols of
+// [K/G][N] fp16.
+static void check_step_copies(int g, int kc, int nk, int N, int K, int sms, int G) {
+    const int NB = N / 16, KC = K / 64;
+    CHECK(kc >= 0 && kc < KC, "weight/activation chunk coordinate %d of %d", kc, KC);
+    CHECK(g * kDcBlocks >= 0 && g * kDcBlocks < NB, "weight block coordinate %d of %d", g * kDcBlocks, NB);
+    // the innermost coordinate of the word and activation copies is always 0
+    const long long col = (long long)g * kDcCols;
+    CHECK(col < N && (col * 2) % 16 == 0, "scale column %lld (N = %d)", col, N);
+    for (int j = 0; j < nk; ++j) {
+        const int row = ((kc + j) * 64) / G;
+        CHECK(row >= 0 && row < K / G, "scale row %d of %d", row, K / G);
+    }
+}
+
 static void check_shape(int N, int K, int sms) {
     ++g_cases;
     const int fails_before = g_fail;
@@ -90,6 +110,8 @@ static void check_shape(int N, int K, int sms) {
         while (st.more()) {
             const int nk = st.nk(KC);
             CHECK(nk >= 1 && nk <= kDcStep && st.kc + nk <= KC && st.pos + nk <= st.end, "step of %d chunks", nk);
+            for (int G : {64, 128})
+                if (K % G == 0) check_step_copies(st.g, st.kc, nk, N, K, sms, G);
             for (int j = 0; j < nk; ++j) {
                 const int u = st.g * KC + st.kc + j;
                 CHECK(u == st.pos + j, "unit order");
