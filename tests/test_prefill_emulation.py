@@ -1,0 +1,150 @@
+"""CPU emulation of prefill_kernel's index mapping, checked against the oracle.
+
+The counterpart, for this package's tcgen05 prefill kernel, of the reference's numpy
+emulation of its own prefill kernel (akshay919191/W4A16-GEMM tests/layout_prefill.py).
+One CTA walks every (token tile, 128-row tile) and every 64-wide k-step as prefill_kernel
+does (csrc/prefill.cuh):
+
+* Dequant warps 2..9 each take n16 block `nbl = 2 (warp & 3) + (qi & 1)` of the step's
+  packed words and scales. They dequantise with the kernel's bit tricks and store the 16
+  registers with `tcgen05.st.16x128b.x8` into the A ring: TMEM lane base 16 nbl, columns
+  A_COL0 + slot * 32.
+* The MMA of each 16-wide k slice reads A from TMEM columns + 8 k16. It reads B as the
+  step's activation rows, through a K-major 128-byte-swizzle descriptor advanced by 32 bytes
+  per slice. It accumulates into columns b * TOK of the fp32 accumulator, overwriting on
+  the first slice of a tile.
+* Epilogue warp (quarter q = warp & 3, part h) reads TMEM lanes 32q..32q+31 and token
+  columns h * TOK/4 .. and stores row n = 128 tn + 32q + lane, tokens 128 tt + ...,
+  guarded by N and M.
+
+Hardware facts assumed, from the PTX ISA:
+* tcgen05.st .16x128b: thread T's register 2j goes to lane T/4, column 4j + T%4, and
+  register 2j+1 to lane T/4 + 8;
+* a warp may access only TMEM lanes 32 (warp % 4) .. +31; the emulation asserts this for
+  every access;
+* an A operand in TMEM holds row i in lane i, two fp16 K elements per column;
+* the swizzled descriptor reads the activation rows as B[k][token] = x[token][k].
+
+The emulation also checks that every A column an MMA reads was written in that k-step,
+that no store touches the accumulator columns, and that every y element is written once.
+"""
+import numpy as np
+import pytest
+
+from oracle import w4a16_oracle as oracle
+
+ROWS, DQ_WARP0, DQ_WARPS, EPI_WARP0, EPI_WARPS = 128, 2, 8, 10, 16
+
+
+def cfg(TOK):
+    accs = 2 if TOK <= 128 else 1
+    a_col0 = accs * TOK
+    return accs, a_col0, min((512 - a_col0) // 32, 8)
+
+
+def dequant16(words, s_lo, s_hi):
+    """dequant_word on a lane's 4 words: 16 32-bit registers, each 2 fp16 (lo, hi)."""
+    regs = []
+    for q in words.astype(np.uint32):
+        q8 = q >> 8
+        for bits, bias, s in ((q & 0x000F000F) | 0x64006400, 1032, s_lo), \
+                             ((q & 0x00F000F0) | 0x54005400, 72, s_hi), \
+                             ((q8 & 0x000F000F) | 0x64006400, 1032, s_lo), \
+                             ((q8 & 0x00F000F0) | 0x54005400, 72, s_hi):
+            lo = np.array([bits & 0xFFFF], np.uint16).view(np.float16)[0] - np.float16(bias)
+            hi = np.array([bits >> 16], np.uint16).view(np.float16)[0] - np.float16(bias)
+            regs.append((np.float16(lo * s), np.float16(hi * s)))
+    return regs
+
+
+def check_lane(warp, lane):
+    assert 32 * (warp % 4) <= lane < 32 * (warp % 4) + 32, f"warp {warp} touched TMEM lane {lane}"
+
+
+def emulate(Wp, x, scales, N, K, G, TOK):
+    M = x.shape[0]
+    NB, KC = N // 16, K // 64
+    Wp4 = Wp.view(np.uint32).reshape(NB, KC, 32, 4)
+    accs, a_col0, na = cfg(TOK)
+    n_tiles, t_tiles = (N + ROWS - 1) // ROWS, (M + TOK - 1) // TOK
+    tmem = np.full((ROWS, 512, 2), np.nan)                  # [lane][column][half]
+    y = np.full((M, N), np.nan)
+    written = np.zeros((M, N), np.int32)
+    it = 0
+    for tc, tile in enumerate(range(n_tiles * t_tiles)):
+        tt, tn = tile // n_tiles, tile % n_tiles
+        b = tc % accs
+        for kt in range(KC):
+            a = it % na
+            it += 1
+            # the stage: packed words of blocks 8 tn .. 8 tn + 7 (zero past N), scale row, x rows
+            words = np.zeros((8, 32, 4), np.uint32)
+            for nbl in range(8):
+                if tn * 8 + nbl < NB:
+                    words[nbl] = Wp4[tn * 8 + nbl, kt]
+            srow = np.zeros(ROWS, np.float16)
+            cols = np.arange(tn * ROWS, tn * ROWS + ROWS)
+            srow[cols < N] = scales[(kt * 64) // G, cols[cols < N]]
+            xt = np.zeros((TOK, 64), np.float64)
+            rows = np.arange(tt * TOK, tt * TOK + TOK)
+            xt[rows < M] = x[rows[rows < M], kt * 64:(kt + 1) * 64]
+            # dequant warps -> TMEM A slot
+            fresh = np.zeros((ROWS, 32), bool)
+            for warp in range(DQ_WARP0, DQ_WARP0 + DQ_WARPS):
+                qi = (warp - 2) >> 2
+                nbl = 2 * (warp & 3) + (qi & 1)
+                for L in range(32):
+                    g = L >> 2
+                    regs = dequant16(words[nbl, L], srow[nbl * 16 + g], srow[nbl * 16 + g + 8])
+                    for R, (lo, hi) in enumerate(regs):
+                        lane = 16 * nbl + L // 4 + 8 * (R % 2)
+                        col = a_col0 + a * 32 + 4 * (R // 2) + (L % 4)
+                        check_lane(warp, lane)
+                        assert a_col0 <= col < 512, "A store outside the A ring"
+                        tmem[lane, col] = (lo, hi)
+                        fresh[lane, col - a_col0 - a * 32] = True
+            assert fresh.all(), "an A column the MMA reads was not written this k-step"
+            # MMA: 4 slices of 16 k
+            for k16 in range(4):
+                cols_a = a_col0 + a * 32 + k16 * 8 + np.arange(8)
+                A = tmem[:, cols_a, :].reshape(ROWS, 16)            # lane i = row i, 2 k per column
+                B = xt[:, k16 * 16:(k16 + 1) * 16].T                # [16 k, TOK]
+                D = tmem[:, b * TOK:(b + 1) * TOK, 0]
+                tmem[:, b * TOK:(b + 1) * TOK, 0] = A @ B + (D if (kt | k16) != 0 else 0.0)
+        # epilogue warps
+        cw = TOK // (EPI_WARPS // 4)
+        for warp in range(EPI_WARP0, EPI_WARP0 + EPI_WARPS):
+            q, h = warp & 3, (warp - EPI_WARP0) >> 2
+            for L in range(32):
+                lane = 32 * q + L
+                check_lane(warp, lane)
+                n = tn * ROWS + 32 * q + L
+                tok0 = tt * TOK + h * cw
+                for j in range(cw):
+                    if n < N and tok0 + j < M:
+                        y[tok0 + j, n] = tmem[lane, b * TOK + h * cw + j, 0]
+                        written[tok0 + j, n] += 1
+    assert (written == 1).all(), "y elements written zero or several times"
+    return y
+
+
+CASES = [
+    # M, N, K, G, TOK: ragged M and N, every token tile, both group sizes
+    (17, 208, 384, 64, 32),
+    (100, 272, 256, 128, 64),
+    (129, 128, 192, 64, 128),
+    (40, 384, 128, 128, 256),
+]
+
+
+@pytest.mark.parametrize("M,N,K,G,TOK", CASES)
+def test_prefill_emulation_matches_oracle(M, N, K, G, TOK):
+    rng = np.random.default_rng(M * 7 + N + K + TOK)
+    q = rng.integers(0, 16, (N, K), dtype=np.uint8)
+    scales = (rng.random((K // G, N)) * 0.018 + 0.002).astype(np.float16)
+    x = rng.standard_normal((M, K)).astype(np.float16)
+    y = emulate(oracle.pack_int4(q), x, scales, N, K, G, TOK)
+    ref = oracle.ref_gemm(x, q, scales, G).astype(np.float64)
+    assert np.isfinite(y).all()
+    err = np.abs(y - ref).max() / np.abs(ref).max()
+    assert err < 1e-5, err
