@@ -240,3 +240,26 @@ def test_decode_emulation_matches_oracle(M, N, K, G, sms):
     assert np.isfinite(y).all(), "an output was not written, or garbage leaked into it"
     err = np.abs(y - ref).max() / np.abs(ref).max()
     assert err < 1e-5, err
+
+
+def _header_ints(path, names):
+    """Integer constants as the kernel sources define them (`constexpr int kX = 16;`)."""
+    import os
+    import re
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "w4a16-gemm_b200", "csrc", path)).read()
+    out = {}
+    for name in names:
+        m = re.search(r"constexpr int %s = (\d+);" % name, src)
+        assert m, f"{name} not found as a literal in {path}"
+        out[name] = int(m.group(1))
+    return out
+
+
+def test_emulation_constants_match_kernel_sources():
+    """The emulation's constants are the kernel's: a change there must be mirrored here."""
+    part = _header_ints("decode_partition.h", ["kDcBlocks", "kDcStep", "kDcMaxCTAs", "kDcMinUnits"])
+    assert (part["kDcBlocks"], part["kDcStep"], part["kDcMaxCTAs"], part["kDcMinUnits"]) == \
+        (BLOCKS, STEP, MAX_CTAS, MIN_UNITS)
+    assert _header_ints("decode.cuh", ["kDcBPW"])["kDcBPW"] == BPW
+    assert BLOCKS // BPW == WARPS and BLOCKS * 16 == COLS

@@ -14,8 +14,8 @@ does (csrc/prefill.cuh):
   per slice. It accumulates into columns b * TOK of the fp32 accumulator, overwriting on
   the first slice of a tile.
 * Epilogue warp (quarter q = warp & 3, part h) reads TMEM lanes 32q..32q+31 and token
-  columns h * TOK/4 .. and stores row n = 128 tn + 32q + lane, tokens 128 tt + ...,
-  guarded by N and M.
+  columns h * TOK/4 .. (h + 1) * TOK/4 - 1 and stores row n = 128 tn + 32q + lane,
+  tokens TOK tt + h * TOK/4 + j, guarded by N and M.
 
 Hardware facts assumed, from the PTX ISA:
 * tcgen05.st .16x128b: thread T's register 2j goes to lane T/4, column 4j + T%4, and
@@ -148,3 +148,23 @@ def test_prefill_emulation_matches_oracle(M, N, K, G, TOK):
     assert np.isfinite(y).all()
     err = np.abs(y - ref).max() / np.abs(ref).max()
     assert err < 1e-5, err
+
+
+def test_emulation_constants_match_kernel_sources():
+    """The emulation's warp layout and TMEM plan are the kernel's (csrc/prefill.cuh)."""
+    import os
+    import re
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "w4a16-gemm_b200", "csrc", "prefill.cuh")).read()
+
+    def define(name):
+        return int(re.search(r"#define %s (\d+)" % name, src).group(1))
+
+    phases, epi = define("W4A16_PF_DQ_PHASES"), define("W4A16_PF_EPI_WARPS")
+    assert (2, 8 * phases, 2 + 8 * phases, epi) == (DQ_WARP0, DQ_WARPS, EPI_WARP0, EPI_WARPS)
+    assert int(re.search(r"constexpr int kPfRows = (\d+);", src).group(1)) == ROWS
+    assert "ACCS = TOK <= 128 ? 2 : 1" in src and "A_COL0 = ACCS * TOK" in src
+    assert "(512 - A_COL0) / 32 < 8 ? (512 - A_COL0) / 32 : 8" in src
+    assert "const int nbl = 2 * (warp & 3) + (qi & 1);" in src
+    assert "tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * 32), r);" in src
+    assert "tc_mma_ts(d, at + k16 * 8, pf_sw128_desc(xa + k16 * 32), idesc, (kt | k16) != 0);" in src
