@@ -263,3 +263,25 @@ def test_emulation_constants_match_kernel_sources():
         (BLOCKS, STEP, MAX_CTAS, MIN_UNITS)
     assert _header_ints("decode.cuh", ["kDcBPW"])["kDcBPW"] == BPW
     assert BLOCKS // BPW == WARPS and BLOCKS * 16 == COLS
+
+
+def test_emulation_index_expressions_match_kernel_source():
+    """The addressing the emulation restates is the kernel's, expression for expression."""
+    import os
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "w4a16-gemm_b200", "csrc", "decode.cuh")).read()
+    for line in [
+        "const uint32_t w_lane = (uint32_t)warp * BPW * w_blk + lane * 16;",
+        "const uint32_t x_lane0 = C::W_BYTES + xr * 128 + ((xu ^ xr) << 4);",
+        "const uint32_t x_lane1 = C::W_BYTES + xr * 128 + (((xu + 4) ^ xr) << 4);",
+        "const uint32_t s_lane = (uint32_t)(C::W_BYTES + C::X_BYTES + warp * BPW * 32 + g8 * 2);",
+        "wv[jj][bb] = lds128(wb + (jb + jj) * 512 + bb * w_blk);",
+        "const uint32_t xa = sb + (jb + jj) * C::X_CHUNK + mt * 1024;",
+        "mma_16816(acc[bb][(jb + jj) % CH][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);",
+        "const int colb = (warp * BPW + bb) * 16 + g8;",
+        "const int tok = mt * 8 + 2 * t4 + (i & 1);",
+        "const int dc = 8 * (i >> 1);",
+        "const bool whole = st.kc + nk == KC && gkc0 == 0;",
+        "v[i] = c <= cl ? __ldcg(p + (size_t)(c == cf ? slot_f : 2 * c) * kDcSlotFloats) : 0.f;",
+    ]:
+        assert line in src, line
