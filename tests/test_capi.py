@@ -149,3 +149,41 @@ def test_header_layout_matches_ctypes(tmp_path):
         assert int(out[name]) == code, name
     assert int(out["W4A16_OUT_F32"]) == capi.W4A16_OUT_F32
     assert int(out["W4A16_ABI_VERSION"]) == capi.load().w4a16_abi_version()
+
+
+@pytest.mark.skipif(__import__("shutil").which("gcc") is None, reason="needs gcc")
+def test_plain_c_client_links_and_validates(tmp_path):
+    """A C99 program links libw4a16.so and gets the reference's validation statuses and
+    messages (kernel.cu:219-249) through the C ABI, with no Python or torch involved."""
+    import subprocess
+    src = tmp_path / "client.c"
+    src.write_text(r'''
+#include <stdio.h>
+#include <string.h>
+#include "w4a16.h"
+int main(void) {
+    int bad = 0;
+    if (w4a16_abi_version() != W4A16_ABI_VERSION) bad |= 1;
+    /* K not a multiple of 64 */
+    w4a16_status s = w4a16_validate(NULL, NULL, NULL, 1, 64, 100, 1, 64 * 100 / 8, -1);
+    if (s != W4A16_ERR_K_MULTIPLE || !strstr(w4a16_last_error(), "multiple of 64")) bad |= 2;
+    /* unsupported group size: K = 512 in 2 groups -> G = 256 */
+    s = w4a16_validate(NULL, NULL, NULL, 1, 64, 512, 2, 64 * 512 / 8, -1);
+    if (s != W4A16_ERR_GROUP_SIZE || !strstr(w4a16_last_error(), "unsupported group size")) bad |= 4;
+    /* variant out of range */
+    s = w4a16_validate(NULL, NULL, NULL, 1, 64, 512, 4, 64 * 512 / 8, 9);
+    if (s != W4A16_ERR_VARIANT || !strstr(w4a16_last_error(), "variant")) bad |= 8;
+    /* valid shape, null pointers: rejected before any device work */
+    s = w4a16_gemm(NULL, NULL, NULL, NULL, 1, 64, 512, 4, 64 * 512 / 8, -1, W4A16_OUT_F16, NULL, 0, NULL);
+    if (s != W4A16_ERR_NULL_POINTER) bad |= 16;
+    if (strcmp(w4a16_status_string(W4A16_OK), "W4A16_OK") != 0) bad |= 32;
+    printf("%d\n", bad);
+    return bad;
+}
+''')
+    exe = tmp_path / "client"
+    libdir = os.path.dirname(capi.library_path())
+    subprocess.run(["gcc", "-std=c99", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                    "-L", libdir, "-lw4a16", "-Wl,-rpath," + libdir, "-o", str(exe)], check=True)
+    r = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert r.returncode == 0 and r.stdout.strip() == "0", (r.returncode, r.stdout, r.stderr)
