@@ -117,12 +117,16 @@ def _failing_rank_main(rank, world, port, layer, mode, timeout_s, results):
     import datetime
     import time
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
-    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=timeout_s))
+    # rendezvous with a generous timeout (process start-up varies), then run the layers on a
+    # group whose collectives time out quickly
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
+    dist.barrier()
+    group = dist.new_group(ranks=list(range(world)), timeout=datetime.timedelta(seconds=timeout_s))
     from w4a16_opt import tp
     M, N, K, G = 2, 256, 512, 128
     x, q, s, Wp = _problem(M, N, K, G)
     cls = tp.ColumnParallelW4A16 if layer == "col" else tp.RowParallelW4A16
-    mod = cls(Wp, s, N, K, gemm_out=_oracle_gemm_out)
+    mod = cls(Wp, s, N, K, group=group, gemm_out=_oracle_gemm_out)
     if rank != 0:
         if mode == "raise":
             raise RuntimeError("injected failure on rank 1")
