@@ -35,7 +35,9 @@ def test_library_has_no_torch_dependency():
     # The C ABI is usable from any host language: no libtorch/libc10 in its link map.
     import subprocess
     out = subprocess.run(["ldd", capi.library_path()], capture_output=True, text=True).stdout
-    assert "torch" not in out and "c10" not in out
+    # library names only: the hex load addresses ldd prints are random and may contain "c10"
+    names = [line.split()[0] for line in out.splitlines() if line.strip()]
+    assert names and not any("torch" in n or "c10" in n for n in names), names
 
 
 def test_status_strings():
