@@ -69,16 +69,30 @@ def alg_bytes(M, N, K, G):
 
 
 def make_inputs(M, N, K, G, seed, device):
-    """Seeded BASELINE inputs: x fp16 [M,K], q uint8 [N,K] (CPU), scales fp16, packed Wp."""
-    from w4a16_opt import pack_int4
+    """Seeded BASELINE inputs: x fp16 [M,K], q uint8 [N,K] (CPU), scales fp16, packed Wp.
+
+    On "cpu" (the reference arm) nothing of this package is imported: the reference's CPU
+    path takes the codes q directly and Wp is None."""
     gen = torch.Generator().manual_seed(seed)
     x = torch.randn(M, K, generator=gen).half()
     q = torch.randint(0, 16, (N, K), generator=gen, dtype=torch.uint8)
     scales = (torch.rand(K // G, N, generator=gen) * 0.018 + 0.002).half()
     if device == "cpu":
         return x, q, scales, None
+    from w4a16_opt import pack_int4
     Wp = pack_int4(q.to(device))
     return x.to(device), q, scales.to(device), Wp
+
+
+def bench_config(world):
+    """The workload description both arms print (same dict, so the lines compare like for like)."""
+    return {"workload": "configs[1] decode sweep: M in {1,4,8,16} x Llama-3-8B (N x K) "
+                        "4096x4096, 1024x4096, 14336x4096, 4096x14336, G=128",
+            "gemms_per_step": len(DECODE_SHAPES) * len(DECODE_M),
+            "algorithmic_bytes_per_step": sum(alg_bytes(M, N, K, DECODE_G) for _, N, K in DECODE_SHAPES
+                                              for M in DECODE_M),
+            "l2": "inputs larger than L2: 16 distinct weight copies per step vs 126 MB L2",
+            "parallelism": "single GPU" if world == 1 else f"tp{world} (col: k/v, gate/up; row: q/o, down)"}
 
 
 def load_peaks():
@@ -256,7 +270,8 @@ def run_ours(args):
             else:
                 layer = tp.RowParallelW4A16(Wp, s, N, K)
                 u.update(layer=layer, x_local=layer.x_slice(x),
-                         part=torch.empty(M, N, dtype=torch.float32, device="cuda"))
+                         part=torch.empty(M, N, dtype=torch.float32, device="cuda"),
+                         y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
                 del u["Wp"]
             units.append(u)
             step_bytes += alg_bytes(M, N, K, DECODE_G)
@@ -272,46 +287,63 @@ def run_ours(args):
             u["layer"].workspace = ws
     torch.cuda.synchronize()
 
-    def step():
-        for u in units:
-            if world == 1:
-                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws)
-            elif "x_local" in u:
-                u["layer"].partial(u["x_local"], out=u["part"])
-                u["layer"].reduce(u["part"])
-            else:
-                u["layer"].local(u["x"], out=u["y_local"])
-                u["layer"].gather(u["y_local"], out=u["y"])
+    def make_step(resident):
+        def step():
+            for u in units:
+                if world == 1:
+                    w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws, weights_resident=resident)
+                elif "x_local" in u:
+                    u["layer"].partial(u["x_local"], out=u["part"])
+                    u["layer"].reduce(u["part"], out=u["y"])
+                else:
+                    u["layer"].local(u["x"], out=u["y_local"])
+                    u["layer"].gather(u["y_local"], out=u["y"])
+        return step
 
-    # kernels of ours per step: each GEMM is decode_kernel (+ decode_combine_kernel when a column
-    # group is split across CTAs), as the route query reports
+    # kernels of ours per step: one decode_kernel per GEMM, as the route query reports
     launches_per_step = 0
     for u in units:
         n_loc = u["N"] // (world if "y_local" in u else 1)
         k_loc = u["K"] // (world if "x_local" in u else 1)
         launches_per_step += w4a16_opt.query_route(u["M"], n_loc, k_loc, k_loc // DECODE_G)["launches"]
 
+    # headline: weights resident (loaded once, as in serving); the GEMMs stream them while
+    # the previous GEMM finishes.  The default stream-ordered mode is measured right after.
     with ClockSampler(smi_index(local)) as clocks:
-        ms = graph_time_ms(step, args.steps, args.warmup, world)
+        ms = graph_time_ms(make_step(True), args.steps, args.warmup, world)
     ms_step = ms / args.steps
     value = step_bytes * args.steps / (ms / 1e3) / 1e9
+    ms_default = graph_time_ms(make_step(False), args.steps, args.warmup, world)
+    default_mode = {"value": round(step_bytes * args.steps / (ms_default / 1e3) / 1e9, 2), "unit": "GB/s",
+                    "ms_per_step": round(ms_default / args.steps, 5),
+                    "mode": "plain stream order: each GEMM reads its weights only after the previous kernel "
+                            "on the stream has completed (w4a16_gemm default)"}
 
-    # ---- e2e through the public API: pinned host activations in, results out, every step
-    e2e = None
+    # ---- e2e through the public API: each step copies its activations in from pinned host
+    # memory (one transfer), makes the 16 calls into one output buffer, reads it back (one
+    # transfer) and synchronises; host wall time
+    e2e, host_us = None, None
     if world == 1:
-        host_x = [u["x"].cpu().pin_memory() for u in units]
-        host_y = [torch.empty(u["M"], u["N"], dtype=torch.float16).pin_memory() for u in units]
-        dev_x = [torch.empty_like(u["x"]) for u in units]
+        x_off, y_off = [0], [0]
+        for u in units:
+            x_off.append(x_off[-1] + u["x"].numel())
+            y_off.append(y_off[-1] + u["M"] * u["N"])
+        host_x = torch.cat([u["x"].flatten() for u in units]).cpu().pin_memory()
+        dev_x = torch.empty(x_off[-1], dtype=torch.float16, device="cuda")
+        host_y = torch.empty(y_off[-1], dtype=torch.float16).pin_memory()
+        dev_y = torch.empty(y_off[-1], dtype=torch.float16, device="cuda")
+        views = [(u, dev_x[x_off[i]:x_off[i + 1]].view(u["M"], u["K"]), dev_y[y_off[i]:y_off[i + 1]].view(u["M"], u["N"]))
+                 for i, u in enumerate(units)]
 
         def e2e_step():
-            for u, hx, hy, dx in zip(units, host_x, host_y, dev_x):
-                dx.copy_(hx, non_blocking=True)
-                y = w4a16_opt.w4a16_gemm(u["Wp"], dx, u["s"])
-                hy.copy_(y, non_blocking=True)
+            dev_x.copy_(host_x, non_blocking=True)
+            for u, xv, yv in views:
+                w4a16_opt.w4a16_gemm_out(u["Wp"], xv, u["s"], yv, weights_resident=True)
+            host_y.copy_(dev_y, non_blocking=True)
             torch.cuda.current_stream().synchronize()
 
-        e2e_steps = max(3, min(args.steps, 500))
-        for _ in range(max(3, args.warmup // 10)):
+        e2e_steps = max(3, min(args.steps, 2000))
+        for _ in range(max(3, min(args.warmup, 50))):
             e2e_step()
         t0 = time.perf_counter()
         for _ in range(e2e_steps):
@@ -319,7 +351,21 @@ def run_ours(args):
         e2e_s = time.perf_counter() - t0
         e2e = {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
-               "api": "w4a16_opt.w4a16_gemm (eager, current stream)"}
+               "ms_per_step": round(e2e_s * 1e3 / e2e_steps, 4),
+               "api": "w4a16_opt.w4a16_gemm_out(weights_resident=True), eager, current stream; "
+                      "one H2D copy of the step's activations, one D2H copy of its outputs, a sync per step"}
+        # host cost of one eager call (Python + binding + C ABI + launch), GPU work well below it
+        u0 = units[0]
+        for _ in range(200):
+            w4a16_opt.w4a16_gemm_out(u0["Wp"], u0["x"], u0["s"], u0["y"], weights_resident=True)
+        torch.cuda.synchronize()
+        n_calls = 5000
+        t0 = time.perf_counter()
+        for _ in range(n_calls):
+            w4a16_opt.w4a16_gemm_out(u0["Wp"], u0["x"], u0["s"], u0["y"], weights_resident=True)
+        host_us = round((time.perf_counter() - t0) / n_calls * 1e6, 2)
+        torch.cuda.synchronize()
+        del host_x, dev_x, host_y, dev_y, views
 
     peaks, peak_kind = load_peaks()
     traffic = profile_traffic("decode_sweep_traffic")
@@ -327,43 +373,57 @@ def run_ours(args):
                 "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(value / peaks["hbm_gbs"], 4),
                 "peak_source": f"hbm_gbs ({peak_kind})",
                 "traffic": None if traffic is None else traffic.get("decode_kernel_dram_bytes_per_step"),
-                "algorithmic_bytes_per_step": step_bytes}
+                "algorithmic_bytes_per_step": step_bytes,
+                "timing": "CUDA events around the step graph's replays: every GEMM of the step is one "
+                          "decode_kernel launch, so this is the kernel time including the gaps between launches"}
     if world > 1:
         roofline["note"] = "per-rank time includes the NCCL collectives of the TP split"
 
-    # ---- prefill, N = 1
+    # ---- prefill per shape, N = 1: one CUDA graph per (M, N, K, G) over distinct
+    # weight copies (>= 256 MB of weights per graph, twice the L2)
     prefill = None
     if world == 1 and not args.no_prefill:
-        punits, pflops, pbytes = [], 0, 0
+        rows, tot_flops, tot_ms = [], 0.0, 0.0
         for (N, K) in PREFILL_SHAPES:
             for G in PREFILL_G:
                 for M in PREFILL_M:
                     x, q, s, Wp = make_inputs(M, N, K, G, seed, "cuda")
                     seed += 1
-                    punits.append((Wp, x, s, torch.empty(M, N, dtype=torch.float16, device="cuda")))
-                    pflops += 2 * M * N * K
-                    pbytes += alg_bytes(M, N, K, G)
-        torch.cuda.synchronize()
+                    copies = max(2, -(-(256 << 20) // (Wp.numel() * 4)))
+                    ws_list = [(Wp, s)] + [(Wp.clone(), s.clone()) for _ in range(copies - 1)]
+                    y = torch.empty(M, N, dtype=torch.float16, device="cuda")
 
-        def pstep():
-            for Wp, x, s, y in punits:
-                w4a16_opt.w4a16_gemm_out(Wp, x, s, y, workspace=ws)
+                    def pstep(ws_list=ws_list, x=x, y=y):
+                        for w, sc in ws_list:
+                            w4a16_opt.w4a16_gemm_out(w, x, sc, y, weights_resident=True)
 
-        psteps = max(3, args.prefill_steps)
-        pms = graph_time_ms(pstep, psteps, 3, world)
-        tflops = pflops * psteps / (pms / 1e3) / 1e12
+                    reps = max(2, args.prefill_steps // 8)
+                    pms = graph_time_ms(pstep, reps, 2, world) / (reps * copies)
+                    flops = 2.0 * M * N * K
+                    tf = flops / (pms / 1e3) / 1e12
+                    route = w4a16_opt.query_route(M, N, K, K // G)
+                    rows.append({"M": M, "N": N, "K": K, "G": G, "us": round(pms * 1e3, 2), "tflops": round(tf, 1),
+                                 "frac": round(tf / peaks["bf16_tflops"], 4),
+                                 "hbm_gbs": round(alg_bytes(M, N, K, G) / (pms / 1e3) / 1e9, 1),
+                                 "tok_tile": route["tile_m"], "grid": route["grid"]})
+                    tot_flops += flops
+                    tot_ms += pms
+                    del ws_list, x, q, s, Wp, y
+                    torch.cuda.empty_cache()
+        tflops = tot_flops / (tot_ms / 1e3) / 1e12
         prefill = {"workload": "configs[2]: M in {128,512,2048,8192} x (14336x4096, 4096x14336) x G in {64,128}",
-                   "value": round(tflops, 1), "unit": "TFLOP/s", "steps": psteps, "ms_per_step": round(pms / psteps, 4),
-                   "gpu_launches": len(punits) * psteps,
+                   "value": round(tflops, 1), "unit": "TFLOP/s", "ms_per_pass": round(tot_ms, 4),
+                   "timing": "per shape: CUDA graph over distinct weight copies (>= 256 MB), mean per call",
                    "roofline": {"bound": "tensor", "kernel": "w4a16::prefill_kernel", "achieved": round(tflops, 1),
                                 "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                                 "frac": round(tflops / peaks["bf16_tflops"], 4),
                                 "peak_source": f"bf16_tflops burst ({peak_kind}; dense fp16 = bf16 rate)",
-                                "frac_of_sustained": round(tflops / peaks["bf16_tflops_sustained"], 4)}}
-        del punits
+                                "frac_of_sustained": round(tflops / peaks["bf16_tflops_sustained"], 4)},
+                   "per_shape": rows}
 
-    # ---- CPU baseline: the reference's CPU path, one pass over the 16 decode GEMMs (rank 0, N = 1)
-    cpu = None
+    # ---- baselines (rank 0, N = 1): the reference's CPU path on the host cores, and the
+    # reference's own CUDA extension rebuilt for sm_100a on this GPU, same inputs and method
+    cpu, gpu_ref = None, None
     if world == 1 and rank == 0 and not args.no_cpu_baseline:
         cunits = [(u["x"].cpu(), u["q"], u["s"].cpu(), DECODE_G) for u in units]
         threads = os.cpu_count() or 1
@@ -371,6 +431,8 @@ def run_ours(args):
         cpu = {"value": round(step_bytes / secs / 1e9, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                "seconds": round(secs, 2),
                "sample": "one pass over the 16 GEMMs of the decode sweep (fp16 dequant + fp32 matmul, torch CPU)"}
+    if world == 1 and rank == 0 and not args.no_gpu_reference:
+        gpu_ref = gpu_reference_baseline(units, step_bytes, value, prefill, args)
 
     if world > 1:
         import torch.distributed as dist
@@ -378,30 +440,78 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    config = bench_config(world)
+    config.update(timing="CUDA graph of one step, K replays between CUDA events, max over ranks",
+                  weights_resident=True)
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded: x~N(0,1) fp16, q~U{0..15}, scales~U[0.002,0.02] fp16)",
-        "config": {"workload": "configs[1] decode sweep: M in {1,4,8,16} x Llama-3-8B (N x K) "
-                               "4096x4096, 1024x4096, 14336x4096, 4096x14336, G=128",
-                   "gemms_per_step": len(units), "algorithmic_bytes_per_step": step_bytes,
-                   "l2": "inputs larger than L2: 16 distinct weight copies, %d MB per step vs 126 MB L2"
-                         % (step_bytes // 2**20),
-                   "parallelism": "single GPU" if world == 1 else f"tp{world} (col: k/v, gate/up; row: q/o, down)",
-                   "timing": "CUDA graph of one step, K replays between CUDA events, max over ranks"},
-        "e2e": e2e, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
-        "clocks": clocks.summary(), "gpu_launches": launches_per_step * args.steps,
+        "config": config, "default_mode": default_mode,
+        "e2e": e2e, "host_us_per_call": host_us, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
+        "gpu_reference": gpu_ref, "clocks": clocks.summary(), "gpu_launches": launches_per_step * args.steps,
     }
     print(json.dumps(out), flush=True)
     return 0
+
+
+def gpu_reference_baseline(units, step_bytes, value, prefill, args):
+    """The reference's own CUDA extension (src/vectorized: mma.sync decode and prefill kernels),
+    compiled for sm_100a into the checker module oracle/_ref, timed on the same decode sweep
+    and configs[2] shapes with the same CUDA-graph method: a baseline, never the product."""
+    from oracle import build_ref
+    ref = build_ref.load()
+    if ref is None:
+        return {"unavailable": "oracle/_ref/w4a16_ref not built on this machine"}
+
+    def dstep():
+        for u in units:
+            ref.w4a16_gemm(u["Wp"], u["x"], u["s"], -1)
+
+    steps = max(20, min(args.steps, 2000))
+    ms = graph_time_ms(dstep, steps, 3, 1)
+    ref_gbs = step_bytes * steps / (ms / 1e3) / 1e9
+    out = {"impl": "reference src/vectorized built for sm_100a (oracle/_ref)", "value": round(ref_gbs, 2),
+           "unit": "GB/s", "ms_per_step": round(ms / steps, 5), "speedup": round(value / ref_gbs, 3),
+           "workload": "same decode sweep step (16 GEMMs, same inputs), CUDA graph replays"}
+    if prefill is not None:
+        rows, tot_flops, tot_ms = [], 0.0, 0.0
+        seed = 5000
+        for (N, K) in PREFILL_SHAPES:
+            for G in PREFILL_G:
+                for M in PREFILL_M:
+                    x, q, s, Wp = make_inputs(M, N, K, G, seed, "cuda")
+                    seed += 1
+                    copies = max(2, -(-(256 << 20) // (Wp.numel() * 4)))
+                    ws_list = [(Wp, s)] + [(Wp.clone(), s.clone()) for _ in range(copies - 1)]
+
+                    def pstep(ws_list=ws_list, x=x):
+                        for w, sc in ws_list:
+                            ref.w4a16_gemm(w, x, sc, -1)
+
+                    pms = graph_time_ms(pstep, 2, 1, 1) / (2 * copies)
+                    rows.append({"M": M, "N": N, "K": K, "G": G, "us": round(pms * 1e3, 2),
+                                 "tflops": round(2.0 * M * N * K / (pms / 1e3) / 1e12, 1)})
+                    tot_flops += 2.0 * M * N * K
+                    tot_ms += pms
+                    del ws_list, x, q, s, Wp
+                    torch.cuda.empty_cache()
+        ref_tf = tot_flops / (tot_ms / 1e3) / 1e12
+        out["prefill"] = {"value": round(ref_tf, 1), "unit": "TFLOP/s", "speedup": round(prefill["value"] / ref_tf, 3),
+                          "per_shape": rows}
+    return out
 
 
 # ---------------------------------------------------------------------------------------------- reference
 
 def run_reference(args):
     """The reference's CPU implementation of the path (its tests/quant.py dequant + torch
-    matmul, restated in oracle/cpu_reference.py) on this host's cores; rank 0 only."""
+    matmul, restated in oracle/cpu_reference.py) on this host's cores; rank 0 only.
+
+    A step is one pass over the 16 GEMMs of the decode sweep, as in the GPU arm.  When the
+    requested steps would run past about two minutes, each step covers the same leading
+    fraction of every GEMM's output columns instead (a bounded sample of the same work)."""
     world, rank, _ = dist_env()
     if rank != 0:
         return 0
@@ -414,23 +524,34 @@ def run_reference(args):
             x, q, s, _ = make_inputs(M, N, K, DECODE_G, seed, "cpu")
             seed += 1
             units.append((x, q, s, M, N, K))
-    # each step is one GEMM of the sweep, cycling through the 16 (a bounded sample per step)
-    for i in range(args.warmup):
-        x, q, s, *_ = units[i % len(units)]
-        cpu_reference.ref_gemm(x, q, s, DECODE_G)
+
+    def one_pass(frac):
+        nbytes = 0
+        for x, q, s, M, N, K in units:
+            n = N if frac >= 1.0 else max(16, int(N * frac) // 16 * 16)
+            cpu_reference.ref_gemm(x, q[:n], s[:, :n], DECODE_G)
+            nbytes += alg_bytes(M, n, K, DECODE_G)
+        return nbytes
+
+    t0 = time.perf_counter()
+    one_pass(1.0)
+    t_pass = time.perf_counter() - t0
+    frac = min(1.0, 120.0 / max(1e-9, t_pass * (args.steps + args.warmup)))
+    for _ in range(max(0, args.warmup - 1)):
+        one_pass(frac)
     total, t0 = 0, time.perf_counter()
-    for i in range(args.steps):
-        x, q, s, M, N, K = units[i % len(units)]
-        cpu_reference.ref_gemm(x, q, s, DECODE_G)
-        total += alg_bytes(M, N, K, DECODE_G)
+    for _ in range(args.steps):
+        total += one_pass(frac)
     secs = time.perf_counter() - t0
     value = total / secs / 1e9
-    sample = "step i = GEMM i mod 16 of the decode sweep (fp16 dequant + fp32 matmul, torch CPU)"
+    sample = ("each step: one pass over the 16 GEMMs of the decode sweep" if frac >= 1.0 else
+              f"each step: the leading {frac:.3f} of every GEMM's output columns, for the 16 GEMMs of the sweep") + \
+        " (fp16 dequant + fp32 matmul, torch CPU)"
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
            "data": "synthetic (seeded, same inputs as the GPU arm)",
-           "config": {"workload": "configs[1] decode sweep (CPU reference path)", "threads": threads},
+           "config": bench_config(world),
            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
                             "sample": sample},
            "e2e": {"value": round(value, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -447,6 +568,7 @@ def main():
     ap.add_argument("--prefill-steps", type=int, default=40)
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gpu-reference", action="store_true")
     args = ap.parse_args()
     if args.impl == "reference":
         args.steps = 16 if args.steps is None else args.steps

@@ -15,22 +15,27 @@
  * from w4a16_last_error().  No function allocates device memory, so GEMM
  * launches may be captured in CUDA graphs.
  *
- * Workspace: the decode path (M <= 16) splits K across SMs and combines the
- * split partial sums through a caller-provided device workspace of
- * w4a16_workspace_bytes() bytes (256-byte aligned).  It is scratch: a call
- * writes every byte it later reads, so it needs no initialisation, and one
+ * Workspace: the decode path (M <= 16) splits K across SMs and reduces the split
+ * partial sums inside the kernel, through a caller-provided device workspace of
+ * w4a16_workspace_bytes() bytes (256-byte aligned).  It must be zero-filled once
+ * before its first use (cudaMemset); every call leaves the parts that must start at
+ * zero (one arrival word per 256-column group, at its head) at zero again, so one
  * workspace serves any number of calls, of any shapes, issued in stream order.
- * Calls that may run concurrently need separate workspaces.
+ * Calls that may run concurrently need separate workspaces.  If a kernel reports a
+ * timeout through w4a16_device_status, zero the workspace again before reusing it.
+ * The CTAs of one decode launch wait for each other at its end (bounded), so they
+ * must all be able to run at the same time: do not give the GPU to other work that
+ * holds SMs indefinitely while a GEMM runs.
  *
- * Stream order: the decode kernel is launched with programmatic dependent launch
- * and starts fetching Wp and scales before the kernel launched just before it on
- * the stream is known to have finished (x, y and the workspace are touched only
- * after that kernel's writes are visible).  So Wp and scales must not be written
- * by the kernel launched immediately before the GEMM: write them with a copy, with
- * this library's format entry points (which end with an empty kernel for this
- * reason), or put any other kernel launch or a synchronisation in between.  The
- * environment variable W4A16_PDL=0 (read once per process) launches every kernel
- * in plain stream order instead, which lifts this rule and gives up the overlap.
+ * Stream order: each GEMM reads nothing (weights, scales, activations, workspace)
+ * before the kernel launched just before it on the stream has completed and its
+ * writes are visible, whatever that kernel was.  Kernels are launched with
+ * programmatic dependent launch, so the next launch's set-up overlaps the previous
+ * one's tail.  A caller whose weights and scales are resident -- not written by the
+ * kernel launched immediately before the GEMM -- may pass W4A16_FLAG_WEIGHTS_RESIDENT
+ * to w4a16_gemm_ex: the decode kernel then starts streaming them before that
+ * kernel has finished.  The environment variable W4A16_PDL=0 (read once per
+ * process) launches every kernel in plain stream order and ignores the flag.
  *
  * This header replaces the reference's torch-typed entry point
  *     torch::Tensor w4a16_gemm_cuda(Tensor Wp, Tensor x, Tensor scales, int64_t variant)
@@ -47,7 +52,7 @@
 extern "C" {
 #endif
 
-#define W4A16_ABI_VERSION 2
+#define W4A16_ABI_VERSION 3
 
 /* Size of the scratch array built into the library for w4a16_gemm_noalloc
  * (6 MiB per device: the decode path's partials on a GPU of up to 192 SMs). */
@@ -70,8 +75,16 @@ typedef enum w4a16_status {
     W4A16_ERR_DEVICE = 13,           /* current device is not an sm_100 GPU */
     W4A16_ERR_CUDA = 14,             /* a CUDA runtime / driver call failed */
     W4A16_ERR_DEVICE_TIMEOUT = 15,   /* a kernel's bounded wait ran out (see w4a16_device_status) */
-    W4A16_ERR_WORKSPACE = 16         /* workspace missing, too small or misaligned */
+    W4A16_ERR_WORKSPACE = 16,        /* workspace missing, too small or misaligned */
+    W4A16_ERR_FLAGS = 17             /* flags holds bits that are not w4a16_flags values */
 } w4a16_status;
+
+typedef enum w4a16_flags {
+    /* Wp and scales are not written by the kernel launched immediately before this GEMM on
+     * its stream (they were written earlier, copied, or made by this library's format entry
+     * points): the decode kernel may start reading them before that kernel completes. */
+    W4A16_FLAG_WEIGHTS_RESIDENT = 1
+} w4a16_flags;
 
 typedef enum w4a16_out_dtype {
     W4A16_OUT_F16 = 0,               /* y is fp16 [M, N] (the reference's output) */
@@ -93,8 +106,8 @@ typedef struct w4a16_route {
     int32_t stages;     /* pipeline depth */
     int32_t smem_bytes; /* dynamic shared memory per CTA */
     uint64_t workspace_bytes; /* workspace the call needs (see w4a16_workspace_bytes) */
-    int32_t launches;   /* kernels one call launches (decode: 2 when a column group is split
-                           across CTAs -- the combine kernel runs behind the main one) */
+    int32_t launches;   /* kernels one call launches (1: split column groups are reduced
+                           inside the decode kernel) */
     int32_t reserved;
 } w4a16_route;
 
@@ -117,24 +130,34 @@ w4a16_status w4a16_workspace_bytes(int64_t M, int64_t N, int64_t K, int64_t grou
 /* y = x @ W^T on `stream`.  variant: -1 auto, 0 decode kernel (reference decode
  * contract: M <= 16, N % 64 == 0, K % 512 == 0), 1..4 force a prefill tile
  * config.  out_dtype selects fp16 or fp32 y.  Replaces w4a16_gemm_cuda
- * (kernel.cu:218-267); unlike it, y and the workspace are caller-allocated. */
+ * (kernel.cu:218-267); unlike it, y and the workspace are caller-allocated.
+ * Same as w4a16_gemm_ex with flags = 0. */
 w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y,
                         int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
                         int32_t variant, int32_t out_dtype, void* workspace, uint64_t workspace_bytes,
                         void* stream);
+
+/* w4a16_gemm with flags (w4a16_flags bits; 0 = plain stream order).  No counterpart in
+ * the reference: its kernels are launched in plain stream order. */
+w4a16_status w4a16_gemm_ex(const int32_t* Wp, const void* x, const void* scales, void* y,
+                           int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
+                           int32_t variant, int32_t out_dtype, uint32_t flags, void* workspace,
+                           uint64_t workspace_bytes, void* stream);
 
 /* Same GEMM as w4a16_gemm for callers that cannot allocate device memory
  * (fixed device-memory budgets, bindings without a device allocator).  No
  * counterpart in the reference, whose entry point allocates y itself.  The
  * scratch the decode path needs comes from an array of
  * W4A16_NOALLOC_SCRATCH_BYTES built into the library instead of a caller
- * workspace; y stays caller-allocated.  Nothing in it needs to start at zero.
+ * workspace; y stays caller-allocated.  The array is zero-filled when the library
+ * is loaded on a device, and every call leaves its arrival words at zero.
  * Limits: a call whose scratch need exceeds the array fails with
  * W4A16_ERR_WORKSPACE; every call on a device uses the same array, so calls
  * that overlap in time (other streams, other host threads) race -- serialise
- * them.  The first call on each device does a one-time set-up (it looks up the
- * array's device address with that device current), so make it before any
- * stream capture. */
+ * them.  Each call made outside stream capture looks up the array's device
+ * address with the device current (a cheap call); a call under capture uses the
+ * address found by the last call outside it, so make at least one call on each
+ * device before any stream capture. */
 w4a16_status w4a16_gemm_noalloc(const int32_t* Wp, const void* x, const void* scales, void* y,
                                 int64_t M, int64_t N, int64_t K, int64_t groups, int64_t wp_words,
                                 int32_t variant, int32_t out_dtype, void* stream);

@@ -28,7 +28,7 @@ def test_library_loads_and_exports_every_symbol():
     lib = capi.load()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.w4a16_abi_version() == 2
+    assert lib.w4a16_abi_version() == 3
 
 
 def test_library_has_no_torch_dependency():
@@ -122,7 +122,7 @@ def test_binding_exports():
     import w4a16_opt
     for name in ("w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status"):
         assert callable(getattr(w4a16_opt, name))
-    assert w4a16_opt.ABI_VERSION == 2
+    assert w4a16_opt.ABI_VERSION == 3
 
 
 @pytest.mark.skipif(__import__("shutil").which("gcc") is None, reason="needs gcc")

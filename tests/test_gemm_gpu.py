@@ -334,9 +334,11 @@ def test_query_route():
     from w4a16_opt import query_route
     r = query_route(1, 4096, 4096, 32)
     assert r["kernel"] == "decode" and r["grid"] == torch.cuda.get_device_properties(0).multi_processor_count
-    assert r["workspace_bytes"] > 0 and r["launches"] == 2   # 16 groups over 148 CTAs: split
+    # 16 groups over 148 CTAs: split groups, reduced inside the one launch
+    assert r["workspace_bytes"] > 0 and r["launches"] == 1
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    assert query_route(1, 256 * sms, 64, 1)["launches"] == 1   # one whole 256-column group per CTA
+    r = query_route(1, 256 * sms, 64, 1)   # one whole 256-column group per CTA: no workspace
+    assert r["launches"] == 1 and r["workspace_bytes"] == 0
     r = query_route(3, 4112, 4160, 65)
     assert r["kernel"] == "decode"
     r = query_route(2048, 14336, 4096, 32)
@@ -374,17 +376,68 @@ def test_c_abi_direct_call(M):
 
 
 def test_shared_workspace_across_shapes():
-    """One workspace serves calls of different shapes in any order (decode stream-K partials)."""
+    """One workspace serves calls of different shapes in any order (decode stream-K partials):
+    only the arrival words at its head must start at zero, and every call leaves them there."""
     from w4a16_opt import make_workspace, w4a16_gemm_out, workspace_bytes
     shapes = [(1, 4096, 4096), (16, 14336, 4096), (3, 1024, 4096), (8, 28672, 4096), (1, 256, 2048), (5, 4096, 14336)]
     ws = make_workspace(max(workspace_bytes(M, N, K, K // 128) for M, N, K in shapes))
-    ws.fill_(0xFF)   # NaN bit patterns: a call must write every workspace byte it reads
+    words = (max(-(-N // 256) for _, N, _ in shapes) * 4 + 255) // 256 * 256   # one word per 256 columns
+    ws[words:].fill_(0xFF)   # NaN bit patterns: a call must write every partial byte it reads
     for rep in range(2):
         for i, (M, N, K) in enumerate(shapes):
             x, q, s, Wp = make_workload(M, N, K, 128, seed=40 + i)
             y = torch.empty(M, N, dtype=torch.half, device="cuda")
             w4a16_gemm_out(Wp, x, s, y, workspace=ws)
             assert_close(y, ref_gemm(x, q, s, 128))
+            torch.cuda.synchronize()
+            assert int((ws[:words].view(torch.int32) & 0x7FFFFFFF).count_nonzero()) == 0, "arrival counts left set"
+
+
+@pytest.mark.parametrize("M,N,K,G", [(1, 4096, 4096, 128), (16, 14336, 4096, 64), (4, 1024, 4096, 128),
+                                     (40, 1024, 2048, 64)])
+def test_weights_written_by_the_kernel_just_before(M, N, K, G):
+    """Plain stream order, as the reference's kernels have it: each round overwrites Wp and
+    scales with torch kernels, the one writing Wp launched immediately before the GEMM, and
+    the default call must see the new weights."""
+    from w4a16_opt import w4a16_gemm
+    problems = [make_workload(M, N, K, G, seed=s) for s in (1, 2)]
+    x = problems[0][0]
+    Wp, s = torch.empty_like(problems[0][3]), torch.empty_like(problems[0][2])
+    refs = [ref_gemm(x, q, sc, G) for (_, q, sc, _) in problems]
+    zero = torch.zeros((), dtype=torch.int32, device="cuda")
+    for r in range(6):
+        _, _, sc, wp = problems[r % 2]
+        torch.mul(sc, 1.0, out=s)                 # elementwise kernels (not copies): a
+        torch.bitwise_xor(wp, zero, out=Wp)       # kernel writes Wp right before the GEMM
+        y = w4a16_gemm(Wp, x, s)
+        assert_close(y, refs[r % 2])
+
+
+@pytest.mark.parametrize("M,N,K,G", [(1, 4096, 4096, 128), (7, 2048, 4096, 64), (16, 1024, 14336, 128)])
+def test_reference_test_setup_pattern(M, N, K, G):
+    """The reference's make_problem (tests/test_w4a16.py:33-38) quantises and packs with torch
+    on the GPU and calls the GEMM next; the same sequence here, through the torch
+    restatement of the format on CUDA tensors."""
+    from w4a16_opt import w4a16_gemm
+    from w4a16_opt.format import pack_int4, quantize_w4
+    gen = torch.Generator().manual_seed(M + N + K)
+    W = torch.randn(N, K, generator=gen) * 0.02
+    x = torch.randn(M, K, generator=gen).half().cuda()
+    q, scales = quantize_w4(W.double().cuda(), G)     # torch kernels on the GPU
+    Wp = pack_int4(q.to(torch.int16))                 # torch kernels; the last one writes Wp
+    y = w4a16_gemm(Wp, x, scales)
+    assert_close(y, ref_gemm(x, q, scales, G))
+
+
+def test_weights_resident_flag_same_result():
+    """Declaring the weights resident changes when they are fetched, not what is computed."""
+    from w4a16_opt import w4a16_gemm_out
+    for (M, N, K) in [(1, 14336, 4096), (9, 4096, 14336), (300, 1024, 2048)]:
+        x, q, s, Wp = make_workload(M, N, K, 128, seed=N + M)
+        torch.cuda.synchronize()
+        a = w4a16_gemm_out(Wp, x, s, torch.empty(M, N, dtype=torch.half, device="cuda"))
+        b = w4a16_gemm_out(Wp, x, s, torch.empty(M, N, dtype=torch.half, device="cuda"), weights_resident=True)
+        assert torch.equal(a, b)
 
 
 def test_device_status_clean():

@@ -86,6 +86,16 @@ def _rank_main(rank, world, port, M, N, K, G, results):
         y_col = col(x)
         row = tp.RowParallelW4A16(Wp, s, N, K, gemm_out=_oracle_gemm_out)
         y_row = row(row.x_slice(x))
+        # caller-provided outputs: written in place (M = 1 included), twice in a row (the
+        # gather's staging buffer is reused), and the same values as the returned tensors
+        y_col_out = torch.full((M, N), float("nan"), dtype=torch.float16)
+        y_row_out = torch.full((M, N), float("nan"), dtype=torch.float16)
+        for _ in range(2):
+            assert col.gather(col.local(x), out=y_col_out) is y_col_out
+            part = row.partial(row.x_slice(x))
+            assert row.reduce(part, out=y_row_out) is y_row_out
+        assert torch.equal(y_col_out, y_col) and torch.equal(y_row_out, y_row)
+        assert len(col._gather_bufs) == (0 if M == 1 else 1)
         results[rank] = (y_col.float().numpy(), y_row.float().numpy())
     finally:
         dist.destroy_process_group()

@@ -130,19 +130,22 @@ w4a16_status w4a16_validate(const void* Wp, const void* x, const void* scales, i
     return ok();
 }
 
-w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
-                        int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
-                        void* workspace, uint64_t workspace_bytes, void* stream) {
+w4a16_status w4a16_gemm_ex(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
+                           int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
+                           uint32_t flags, void* workspace, uint64_t workspace_bytes, void* stream) {
     w4a16_status s = w4a16_validate(Wp, x, scales, M, N, K, groups, wp_words, variant);
     if (s != W4A16_OK) return s;
     if (!Wp || !x || !scales || !y) return fail(W4A16_ERR_NULL_POINTER, "Wp, x, scales and y must be non-null");
     if (out_dtype != W4A16_OUT_F16 && out_dtype != W4A16_OUT_F32)
         return fail(W4A16_ERR_OUT_DTYPE, "out_dtype must be 0 (fp16) or 1 (fp32)");
+    if (flags & ~(uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT)
+        return fail(W4A16_ERR_FLAGS, "unknown flag bits " + std::to_string(flags & ~(uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT));
     w4a16::DeviceInfo d;
     if ((s = check_device(&d)) != W4A16_OK) return s;
     const int G = (int)(K / groups);
     w4a16::GemmArgs a{Wp, x, scales, y, (int)M, (int)N, (int)K, G, out_dtype == W4A16_OUT_F32,
-                      static_cast<cudaStream_t>(stream), pdl_enabled(), workspace, (size_t)workspace_bytes};
+                      static_cast<cudaStream_t>(stream), pdl_enabled(), (flags & W4A16_FLAG_WEIGHTS_RESIDENT) != 0,
+                      workspace, (size_t)workspace_bytes};
     const Route r = make_route(a.M, a.N, a.K, G, variant, d);
     const size_t need = route_workspace(r);
     if (need > 0) {
@@ -159,6 +162,13 @@ w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, vo
     return ok();
 }
 
+w4a16_status w4a16_gemm(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
+                        int64_t K, int64_t groups, int64_t wp_words, int32_t variant, int32_t out_dtype,
+                        void* workspace, uint64_t workspace_bytes, void* stream) {
+    return w4a16_gemm_ex(Wp, x, scales, y, M, N, K, groups, wp_words, variant, out_dtype, 0u, workspace,
+                         workspace_bytes, stream);
+}
+
 // The GEMM with the library's built-in scratch in place of a caller workspace: the
 // same validation, routing and kernels as w4a16_gemm, which it calls.
 w4a16_status w4a16_gemm_noalloc(const int32_t* Wp, const void* x, const void* scales, void* y, int64_t M, int64_t N,
@@ -172,7 +182,7 @@ w4a16_status w4a16_gemm_noalloc(const int32_t* Wp, const void* x, const void* sc
         return w4a16_gemm(Wp, x, scales, y, M, N, K, groups, wp_words, variant, out_dtype, nullptr, 0, stream);
     void* scratch = nullptr;
     size_t cap = 0;
-    const cudaError_t err = w4a16::noalloc_scratch(&scratch, &cap);
+    const cudaError_t err = w4a16::noalloc_scratch(&scratch, &cap, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
     if (need > cap)
         return fail(W4A16_ERR_WORKSPACE, "this call needs " + std::to_string(need) +
@@ -330,6 +340,7 @@ const char* w4a16_status_string(w4a16_status status) {
         case W4A16_ERR_CUDA: return "W4A16_ERR_CUDA";
         case W4A16_ERR_DEVICE_TIMEOUT: return "W4A16_ERR_DEVICE_TIMEOUT";
         case W4A16_ERR_WORKSPACE: return "W4A16_ERR_WORKSPACE";
+        case W4A16_ERR_FLAGS: return "W4A16_ERR_FLAGS";
     }
     return "W4A16_ERR_UNKNOWN";
 }

@@ -18,7 +18,9 @@ struct GemmArgs {
     bool out_f32;         // fp32 output (tensor-parallel partials) instead of fp16
     cudaStream_t stream;
     bool pdl;             // launch with programmatic dependent launch enabled
-    void* workspace;      // decode scratch (split-group partials); no initial contents needed
+    bool weights_resident;// wp/scales are not written by the kernel launched just before:
+                          // the decode producer may fetch them before griddepcontrol.wait
+    void* workspace;      // decode scratch: split-group arrival words (zero between calls) + partials
     size_t workspace_bytes;
 };
 
@@ -42,11 +44,11 @@ cudaError_t ensure_max_dynamic_smem(const void* func);
 cudaError_t read_device_status(int* code, bool reset);
 
 // Built-in scratch of w4a16_gemm_noalloc: a device array of kNoAllocScratchBytes
-// compiled into the library.  Returns its address on the current device (looked
-// up once per device).
+// compiled into the library.  Returns its address on the current device (looked up
+// on every call outside stream capture; under capture, the last address found).
 constexpr size_t kNoAllocScratchBytes = W4A16_NOALLOC_SCRATCH_BYTES;
 constexpr int kMaxDevices = 64;
-cudaError_t noalloc_scratch(void** ptr, size_t* bytes);
+cudaError_t noalloc_scratch(void** ptr, size_t* bytes, cudaStream_t stream);
 
 // ---------------------------------------------------------------- decode (M <= 16)
 struct DecodePlan {
@@ -56,7 +58,7 @@ struct DecodePlan {
     int stages;       // TMA ring depth
     size_t smem;      // dynamic shared memory bytes
     size_t workspace; // bytes of workspace the launch needs
-    int launches;     // kernels launched: 1, or 2 when a group is split (combine kernel)
+    int launches;     // kernels launched per call (1)
     bool valid;
 };
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);

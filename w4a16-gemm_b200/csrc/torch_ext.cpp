@@ -35,30 +35,47 @@ void check_tensors(const torch::Tensor& Wp, const torch::Tensor& x, const torch:
     TORCH_CHECK(Wp.device() == x.device() && scales.device() == x.device(), "all tensors must be on one device");
 }
 
-// Workspace for the stream-K decode path (scratch, no initialisation needed): one
-// buffer per (device, stream), reused by every call on that stream, since calls
-// on one stream never overlap.  While the stream is being captured into a CUDA
-// graph a fresh buffer is taken from the graph's pool instead.
+// Workspace for the stream-K decode path: zero-filled when allocated, after which every
+// call leaves its arrival words at zero, so one buffer serves every call on a stream
+// (calls on one stream never overlap).  Eager calls use one buffer per (device, stream).
+// While a stream is being captured into a CUDA graph, the calls of that capture share a
+// buffer taken from the graph's pool (its zero fill is captured once); a new capture on
+// the stream releases the previous capture's.  Both maps are capped: streams come and go
+// in serving engines, and a released buffer's memory is only reused in stream order.
 torch::Tensor workspace_for(const torch::Tensor& x, uint64_t bytes, cudaStream_t stream) {
     if (bytes == 0) return torch::Tensor();
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
-    TORCH_CHECK(cudaStreamIsCapturing(stream, &cap) == cudaSuccess, "cudaStreamIsCapturing failed");
+    unsigned long long capture_id = 0;
+    TORCH_CHECK(cudaStreamGetCaptureInfo(stream, &cap, &capture_id) == cudaSuccess, "cudaStreamGetCaptureInfo failed");
     auto opts = torch::TensorOptions().dtype(torch::kUInt8).device(x.device());
-    if (cap != cudaStreamCaptureStatusNone) return torch::empty({(int64_t)bytes}, opts);
+    constexpr size_t kMaxEntries = 64;
     static std::mutex mu;
-    static std::map<std::pair<int, cudaStream_t>, torch::Tensor> cache;
+    static std::map<std::pair<int, cudaStream_t>, torch::Tensor> eager;
+    static std::map<std::pair<int, cudaStream_t>, std::pair<unsigned long long, torch::Tensor>> captured;
+    const auto key = std::make_pair((int)x.get_device(), stream);
     std::lock_guard<std::mutex> lk(mu);
-    auto& ws = cache[{x.get_device(), stream}];
-    if (!ws.defined() || (uint64_t)ws.numel() < bytes) ws = torch::empty({(int64_t)bytes}, opts);
+    if (cap != cudaStreamCaptureStatusNone) {
+        auto it = captured.find(key);
+        if (it != captured.end() && it->second.first == capture_id && (uint64_t)it->second.second.numel() >= bytes)
+            return it->second.second;
+        if (it == captured.end() && captured.size() >= kMaxEntries) captured.clear();
+        auto ws = torch::zeros({(int64_t)bytes}, opts);
+        captured[key] = {capture_id, ws};
+        return ws;
+    }
+    auto it = eager.find(key);
+    if (it != eager.end() && (uint64_t)it->second.numel() >= bytes) return it->second;
+    if (it == eager.end() && eager.size() >= kMaxEntries) eager.clear();
+    auto ws = torch::zeros({(int64_t)bytes}, opts);
+    eager[key] = ws;
     return ws;
 }
 
 void run(const torch::Tensor& Wp, const torch::Tensor& x, const torch::Tensor& scales, torch::Tensor& y,
-         int32_t variant, const c10::optional<torch::Tensor>& user_ws = c10::nullopt) {
+         int32_t variant, const c10::optional<torch::Tensor>& user_ws = c10::nullopt, uint32_t flags = 0) {
     const at::cuda::CUDAGuard guard(x.device());
     cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
     uint64_t ws_bytes = 0;
-    check(w4a16_workspace_bytes(x.size(0), scales.size(1), x.size(1), scales.size(0), variant, &ws_bytes));
     torch::Tensor ws;
     if (user_ws.has_value() && user_ws->defined()) {
         ws = *user_ws;
@@ -66,12 +83,13 @@ void run(const torch::Tensor& Wp, const torch::Tensor& x, const torch::Tensor& s
                     "workspace must be a contiguous CUDA tensor on x's device");
         ws_bytes = (uint64_t)ws.numel() * ws.element_size();
     } else {
+        check(w4a16_workspace_bytes(x.size(0), scales.size(1), x.size(1), scales.size(0), variant, &ws_bytes));
         ws = workspace_for(x, ws_bytes, stream);
     }
-    check(w4a16_gemm(Wp.data_ptr<int32_t>(), x.data_ptr(), scales.data_ptr(), y.data_ptr(), x.size(0),
-                     scales.size(1), x.size(1), scales.size(0), Wp.numel(), variant,
-                     y.scalar_type() == torch::kFloat ? W4A16_OUT_F32 : W4A16_OUT_F16,
-                     ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, stream));
+    check(w4a16_gemm_ex(Wp.data_ptr<int32_t>(), x.data_ptr(), scales.data_ptr(), y.data_ptr(), x.size(0),
+                        scales.size(1), x.size(1), scales.size(0), Wp.numel(), variant,
+                        y.scalar_type() == torch::kFloat ? W4A16_OUT_F32 : W4A16_OUT_F16, flags,
+                        ws.defined() ? ws.data_ptr() : nullptr, ws_bytes, stream));
 }
 
 }  // namespace
@@ -88,10 +106,12 @@ torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor sca
 }
 
 // Same GEMM into a caller-provided contiguous y: fp16, or fp32 for row-parallel partial sums.
-// `workspace` (optional): a CUDA buffer of >= workspace_bytes(...) bytes that the caller
-// keeps for calls issued in stream order; otherwise the binding supplies one.
+// `workspace` (optional): a zero-filled CUDA buffer of >= workspace_bytes(...) bytes that the
+// caller keeps for calls issued in stream order; otherwise the binding supplies one.
+// `weights_resident`: Wp and scales are not written by the kernel launched just before
+// (W4A16_FLAG_WEIGHTS_RESIDENT).
 torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, torch::Tensor y,
-                                int64_t variant, c10::optional<torch::Tensor> workspace) {
+                                int64_t variant, c10::optional<torch::Tensor> workspace, bool weights_resident) {
     check_tensors(Wp, x, scales);
     TORCH_CHECK(y.is_cuda() && y.device() == x.device(), "y must be a CUDA tensor on x's device");
     TORCH_CHECK(y.is_contiguous(), "contiguous only");
@@ -100,7 +120,7 @@ torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor
     const int32_t v = clamp_variant(variant);
     check(w4a16_validate(Wp.data_ptr(), x.data_ptr(), scales.data_ptr(), x.size(0), scales.size(1), x.size(1),
                          scales.size(0), Wp.numel(), v));
-    run(Wp, x, scales, y, v, workspace);
+    run(Wp, x, scales, y, v, workspace, weights_resident ? (uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT : 0u);
     return y;
 }
 
@@ -185,7 +205,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("variant") = -1);
     m.def("w4a16_gemm_out", &w4a16_gemm_out_py, "W4A16 GEMM into a preallocated fp16/fp32 output",
           pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("y"),
-          pybind11::arg("variant") = -1, pybind11::arg("workspace") = pybind11::none());
+          pybind11::arg("variant") = -1, pybind11::arg("workspace") = pybind11::none(),
+          pybind11::arg("weights_resident") = false);
     m.def("workspace_bytes", &workspace_bytes_py, "workspace bytes a GEMM call needs on the current device",
           pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("groups"),
           pybind11::arg("variant") = -1);

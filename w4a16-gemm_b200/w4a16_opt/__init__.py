@@ -46,14 +46,21 @@ def w4a16_gemm(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, variant:
 
 
 def w4a16_gemm_out(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, y: torch.Tensor,
-                   variant: int = -1, workspace: torch.Tensor | None = None) -> torch.Tensor:
+                   variant: int = -1, workspace: torch.Tensor | None = None,
+                   weights_resident: bool = False) -> torch.Tensor:
     """Same GEMM into a preallocated contiguous ``y`` (fp16, or fp32 for partial sums).
 
-    ``workspace``: optional scratch CUDA buffer (see ``make_workspace``; no initialisation
-    needed) reused by calls issued in stream order.  Without it the binding keeps one
-    per (device, stream), or takes a fresh one from the graph pool under capture.
+    ``workspace``: optional CUDA buffer from ``make_workspace`` (zero-filled once; calls keep
+    the parts that must be zero at zero) reused by calls issued in stream order.  Without it
+    the binding keeps one per (device, stream), or one per capture under CUDA-graph capture.
+
+    ``weights_resident``: the caller declares that ``Wp`` and ``scales`` were not written by
+    the kernel launched just before this call on the stream (loaded earlier, copied, or made
+    by this package's format functions).  The decode kernel then starts streaming them
+    before that kernel has finished.  By default the GEMM reads nothing before the previous
+    kernel's writes are visible, as plain stream order promises.
     """
-    return _C.w4a16_gemm_out(Wp, x, scales, y, variant, workspace)
+    return _C.w4a16_gemm_out(Wp, x, scales, y, variant, workspace, weights_resident)
 
 
 def workspace_bytes(M: int, N: int, K: int, groups: int, variant: int = -1) -> int:
@@ -62,7 +69,7 @@ def workspace_bytes(M: int, N: int, K: int, groups: int, variant: int = -1) -> i
 
 
 def make_workspace(nbytes: int, device=None) -> torch.Tensor:
-    """A workspace buffer of at least ``nbytes`` bytes (zero-filled, though no call needs that)."""
+    """A zero-filled workspace buffer of at least ``nbytes`` bytes (the state calls expect)."""
     return torch.zeros(max(256, int(nbytes)), dtype=torch.uint8, device=device or "cuda")
 
 

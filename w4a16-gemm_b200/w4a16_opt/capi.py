@@ -15,13 +15,14 @@ import os
 W4A16_OK = 0
 W4A16_OUT_F16 = 0
 W4A16_OUT_F32 = 1
+W4A16_FLAG_WEIGHTS_RESIDENT = 1
 
 STATUS_NAMES = {
     0: "W4A16_OK", 1: "W4A16_ERR_NULL_POINTER", 2: "W4A16_ERR_VARIANT", 3: "W4A16_ERR_M",
     4: "W4A16_ERR_DIM_RANGE", 5: "W4A16_ERR_K_MULTIPLE", 6: "W4A16_ERR_N_MULTIPLE", 7: "W4A16_ERR_GROUPS",
     8: "W4A16_ERR_WP_SIZE", 9: "W4A16_ERR_ALIGNMENT", 10: "W4A16_ERR_GROUP_SIZE",
     11: "W4A16_ERR_DECODE_SHAPE", 12: "W4A16_ERR_OUT_DTYPE", 13: "W4A16_ERR_DEVICE", 14: "W4A16_ERR_CUDA",
-    15: "W4A16_ERR_DEVICE_TIMEOUT", 16: "W4A16_ERR_WORKSPACE",
+    15: "W4A16_ERR_DEVICE_TIMEOUT", 16: "W4A16_ERR_WORKSPACE", 17: "W4A16_ERR_FLAGS",
 }
 
 
@@ -39,6 +40,8 @@ EXPORTS = {
     "w4a16_validate": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32]),
     "w4a16_workspace_bytes": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_u64)]),
     "w4a16_gemm": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp, _u64, _vp]),
+    "w4a16_gemm_ex": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, ctypes.c_uint32, _vp,
+                             _u64, _vp]),
     "w4a16_gemm_noalloc": (_i32, [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _i64, _i32, _i32, _vp]),
     "w4a16_query_route": (_i32, [_i64, _i64, _i64, _i64, _i32, ctypes.POINTER(Route)]),
     "w4a16_dequant": (_i32, [_vp, _vp, _vp, _i64, _i64, _i64, _vp]),

@@ -28,13 +28,14 @@ GemmOut = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], tor
 
 
 def _default_gemm_out(Wp, x, scales, y, workspace=None):
+    # the shards were made once, at construction, and settled: resident weights
     from . import w4a16_gemm_out
-    return w4a16_gemm_out(Wp, x, scales, y, workspace=workspace)
+    return w4a16_gemm_out(Wp, x, scales, y, workspace=workspace, weights_resident=True)
 
 
 def _settle(*tensors: torch.Tensor) -> None:
-    """Wait for the copies that made CUDA shards.  The GEMM reads weights before its
-    dependent-launch wait, so they must not come from the kernel launched just before it."""
+    """Wait for the copies that made CUDA shards, so that every later GEMM may declare them
+    resident (fetched before the previous kernel on the stream has finished)."""
     for t in tensors:
         if t.is_cuda:
             torch.cuda.current_stream(t.device).synchronize()
@@ -78,6 +79,7 @@ class ColumnParallelW4A16:
         self.Wp, self.scales = shard_columns(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
         self.workspace: Optional[torch.Tensor] = None   # optional GEMM workspace (scratch)
+        self._gather_bufs: dict = {}
 
     def local(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         y = out if out is not None else torch.empty(x.shape[0], self.N_local, dtype=torch.float16, device=x.device)
@@ -89,13 +91,21 @@ class ColumnParallelW4A16:
         return self.gemm_out(self.Wp, x, self.scales, y)
 
     def gather(self, y_local: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """y [M, N] from every rank's y_local [M, N/P]; written into ``out`` when given."""
         M = y_local.shape[0]
-        # ranks' blocks concatenated along dim 0 ([world * M, N/P]: the layout every backend takes)
-        buf = torch.empty(self.world * M, self.N_local, dtype=y_local.dtype, device=y_local.device)
-        dist.all_gather_into_tensor(buf, y_local.contiguous(), group=self.group)
-        if M == 1:
-            return buf.view(1, self.N)
         y = out if out is not None else torch.empty(M, self.N, dtype=y_local.dtype, device=y_local.device)
+        if M == 1:
+            # one token: the ranks' blocks concatenated are already y's row
+            dist.all_gather_into_tensor(y.view(-1), y_local.contiguous().view(-1), group=self.group)
+            return y
+        # ranks' blocks concatenated along dim 0 ([world * M, N/P]: the layout every backend
+        # takes) into a staging buffer kept per (M, dtype), then one strided copy into y
+        key = (M, y_local.dtype, y_local.device)
+        buf = self._gather_bufs.get(key)
+        if buf is None:
+            buf = torch.empty(self.world * M, self.N_local, dtype=y_local.dtype, device=y_local.device)
+            self._gather_bufs[key] = buf
+        dist.all_gather_into_tensor(buf, y_local.contiguous(), group=self.group)
         y.view(M, self.world, self.N_local).copy_(buf.view(self.world, M, self.N_local).permute(1, 0, 2))
         return y
 
@@ -126,9 +136,13 @@ class RowParallelW4A16:
             return self.gemm_out(self.Wp, x_local, self.scales, y, workspace=self.workspace)
         return self.gemm_out(self.Wp, x_local, self.scales, y)
 
-    def reduce(self, partial: torch.Tensor) -> torch.Tensor:
+    def reduce(self, partial: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Sums the ranks' fp32 partials in place, then casts to fp16 (into ``out`` when given)."""
         dist.all_reduce(partial, op=dist.ReduceOp.SUM, group=self.group)
-        return partial.half()
+        if out is None:
+            return partial.half()
+        out.copy_(partial)
+        return out
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
         return self.reduce(self.partial(x_local))
