@@ -10,9 +10,10 @@ is the reference implementation.  GPU parity tests compare the product against
 it on the same inputs.  Nothing here is imported by the product, and no
 reference source is copied into this repository.
 
-The reference directory comes from $W4A16_REFERENCE_DIR (default: the mounted
-reference checkout).  Without it (as on a GPU box, which only receives the
-prebuilt module) this is a no-op.
+The reference directory comes from the ``reference_dir`` argument or
+$W4A16_REFERENCE_DIR; there is no default.  Without either, or where the directory
+is absent (as on a GPU box, which only receives the prebuilt module), this is a
+no-op.
 """
 from __future__ import annotations
 
@@ -28,8 +29,9 @@ OUT_PATH = os.path.join(OUT_DIR, MODULE + sysconfig.get_config_var("EXT_SUFFIX")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 
-def reference_dir():
-    return os.environ.get("W4A16_REFERENCE_DIR", "/root/reference")
+def reference_dir(explicit=None):
+    """The reference checkout: the argument, else $W4A16_REFERENCE_DIR, else None."""
+    return explicit or os.environ.get("W4A16_REFERENCE_DIR") or None
 
 
 def _run(cmd):
@@ -37,8 +39,8 @@ def _run(cmd):
     subprocess.run(cmd, check=True)
 
 
-def build(force=False):
-    src = os.path.join(reference_dir(), "src", "vectorized")
+def build(force=False, ref_dir=None):
+    src = os.path.join(reference_dir(ref_dir), "src", "vectorized")
     kernel, ext = os.path.join(src, "kernel.cu"), os.path.join(src, "extension.cpp")
     deps = [kernel, ext] + [os.path.join(src, h) for h in ("common.cuh", "decode.cuh", "prefill.cuh")]
     if not force and os.path.exists(OUT_PATH) and all(os.path.getmtime(d) <= os.path.getmtime(OUT_PATH) for d in deps):
@@ -66,13 +68,14 @@ def build(force=False):
     return OUT_PATH
 
 
-def build_if_available(force=False):
+def build_if_available(force=False, ref_dir=None):
     """Build when the reference sources are present; report and skip otherwise."""
-    if not os.path.isdir(os.path.join(reference_dir(), "src", "vectorized")):
+    root = reference_dir(ref_dir)
+    if not root or not os.path.isdir(os.path.join(root, "src", "vectorized")):
         print("oracle/build_ref.py: reference sources not present; skipping (prebuilt module used if any)")
         return None
     try:
-        return build(force)
+        return build(force, root)
     except (subprocess.CalledProcessError, OSError) as exc:   # checker only: never blocks the product build
         print(f"oracle/build_ref.py: reference extension did not build: {exc}")
         return None
@@ -96,5 +99,6 @@ def load():
 if __name__ == "__main__":
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
+    ap.add_argument("--reference", default=None, help="reference checkout (else $W4A16_REFERENCE_DIR)")
     a = ap.parse_args()
-    print(build_if_available(a.force))
+    print(build_if_available(a.force, a.reference))

@@ -54,9 +54,12 @@ def sha(t: torch.Tensor) -> str:
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default=os.environ.get("W4A16_REF", "/root/reference"))
+    ap.add_argument("--ref", default=os.environ.get("W4A16_REF"),
+                    help="reference checkout to import tests/quant.py from (or $W4A16_REF)")
     ap.add_argument("--out", default=os.path.join(HERE, "golden.npz"))
     args = ap.parse_args()
+    if not args.ref:
+        ap.error("pass --ref <reference checkout> or set W4A16_REF")
     rq = load_reference_quant(args.ref)
     out = {}
 

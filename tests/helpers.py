@@ -65,7 +65,8 @@ def ref_gemm(x, q, scales, G, rows=None):
 
 def assert_close(y, ref, tol=2e-3):
     """Reference criterion (tests/test_w4a16.py:41-44) plus the north-star tolerance:
-    max|d| / max|ref| < tol, rel. Frobenius error <= 1e-3, max|d| <= 5e-3 * max|ref|."""
+    max|d| / max|ref| < tol (the reference's 2e-3, relaxed by its own tests to 4e-3 for hard
+    scale ranges), and always relative Frobenius error <= 1e-3 and max|d| <= 5e-3 * max|ref|."""
     yf = to_np(y).astype(np.float32) if isinstance(y, torch.Tensor) else np.asarray(y, np.float32)
     ref = np.asarray(ref, np.float32)
     assert np.isfinite(yf).all(), "NaN/Inf in output"
@@ -77,5 +78,5 @@ def assert_close(y, ref, tol=2e-3):
     rel = float(d.max()) / denom
     assert rel < tol, f"max-abs error / max|ref| = {rel:.3e} (tol {tol:.0e})"
     fro = float(np.linalg.norm(yf - ref) / max(np.linalg.norm(ref), 1e-30))
-    assert fro <= 1e-3 * (tol / 2e-3), f"relative Frobenius error {fro:.3e}"
-    assert float(d.max()) <= 5e-3 * denom * (tol / 2e-3), "max|d| > 5e-3 * max|y_ref|"
+    assert fro <= 1e-3, f"relative Frobenius error {fro:.3e}"
+    assert float(d.max()) <= 5e-3 * denom, "max|d| > 5e-3 * max|y_ref|"

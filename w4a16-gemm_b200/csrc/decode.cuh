@@ -71,7 +71,7 @@ struct DcCfg {
     static constexpr int SROW = kDcCols * 2;                      // one chunk's scales of the group (512 B)
     static constexpr int S_BYTES = kDcStep * SROW;
     static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + S_BYTES;
-    static constexpr int BAR_BYTES = 2 * ST * 8;
+    static constexpr int BAR_BYTES = 2 * ST * 8 + 16;              // full/empty barriers + 2 go flags
     static constexpr int SMEM = 1024 + ST * STAGE_BYTES + BAR_BYTES;
     static_assert(STAGE_BYTES % 1024 == 0 && X_CHUNK % 1024 == 0, "stage alignment (128-byte swizzle atoms)");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -370,7 +370,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
 
     // ------------------------------------------------ split groups: arrive, then reduce this CTA's slice
     if (npend == 0) return;
-    __shared__ uint32_t s_go[2];
+    volatile uint32_t* const s_go = reinterpret_cast<volatile uint32_t*>(smem_raw + (bars - raw) + 2 * ST * 8);
     // Every consumer warp gets here, also after a timed-out wait (the others then time out
     // too); the barrier orders every consumer's partial stores before the arrival and makes
     // the go / no-go decision the same for the whole CTA.

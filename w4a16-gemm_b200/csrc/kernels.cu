@@ -51,7 +51,11 @@ cudaError_t ensure_max_dynamic_smem(const void* func) {
     if (err != cudaSuccess) return err;
     std::lock_guard<std::mutex> lk(mu);
     if (done.count({func, d.device})) return cudaSuccess;
-    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, d.max_smem_optin);
+    // the opt-in maximum covers static and dynamic shared memory together
+    cudaFuncAttributes fa;
+    if ((err = cudaFuncGetAttributes(&fa, func)) != cudaSuccess) return err;
+    err = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               d.max_smem_optin - (int)fa.sharedSizeBytes);
     // all of the unified L1/shared array as shared memory (the kernels stage through it)
     if (err == cudaSuccess)
         err = cudaFuncSetAttribute(func, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
