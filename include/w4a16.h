@@ -15,17 +15,12 @@
  * from w4a16_last_error().  No function allocates device memory, so GEMM
  * launches may be captured in CUDA graphs.
  *
- * Workspace: the decode path (M <= 16) splits K across SMs and reduces the split
- * partial sums inside the kernel, through a caller-provided device workspace of
- * w4a16_workspace_bytes() bytes (256-byte aligned).  It must be zero-filled once
- * before its first use (cudaMemset); every call leaves the parts that must start at
- * zero (one arrival word per 256-column group, at its head) at zero again, so one
+ * Workspace: the decode path (M <= 16) may split K across SMs and combine the
+ * split partial sums through a caller-provided device workspace of
+ * w4a16_workspace_bytes() bytes (256-byte aligned).  It is scratch: a call
+ * writes every byte it later reads, so it needs no initialisation, and one
  * workspace serves any number of calls, of any shapes, issued in stream order.
- * Calls that may run concurrently need separate workspaces.  If a kernel reports a
- * timeout through w4a16_device_status, zero the workspace again before reusing it.
- * The CTAs of one decode launch wait for each other at its end (bounded), so they
- * must all be able to run at the same time: do not give the GPU to other work that
- * holds SMs indefinitely while a GEMM runs.
+ * Calls that may run concurrently need separate workspaces.
  *
  * Stream order: each GEMM reads nothing (weights, scales, activations, workspace)
  * before the kernel launched just before it on the stream has completed and its
@@ -106,8 +101,8 @@ typedef struct w4a16_route {
     int32_t stages;     /* pipeline depth */
     int32_t smem_bytes; /* dynamic shared memory per CTA */
     uint64_t workspace_bytes; /* workspace the call needs (see w4a16_workspace_bytes) */
-    int32_t launches;   /* kernels one call launches (1: split column groups are reduced
-                           inside the decode kernel) */
+    int32_t launches;   /* kernels one call launches (decode: 2 when a column group is split
+                           across CTAs -- the combine kernel runs behind the main one) */
     int32_t reserved;
 } w4a16_route;
 
@@ -149,8 +144,7 @@ w4a16_status w4a16_gemm_ex(const int32_t* Wp, const void* x, const void* scales,
  * counterpart in the reference, whose entry point allocates y itself.  The
  * scratch the decode path needs comes from an array of
  * W4A16_NOALLOC_SCRATCH_BYTES built into the library instead of a caller
- * workspace; y stays caller-allocated.  The array is zero-filled when the library
- * is loaded on a device, and every call leaves its arrival words at zero.
+ * workspace; y stays caller-allocated.  Nothing in it needs to start at zero.
  * Limits: a call whose scratch need exceeds the array fails with
  * W4A16_ERR_WORKSPACE; every call on a device uses the same array, so calls
  * that overlap in time (other streams, other host threads) race -- serialise

@@ -1,15 +1,13 @@
 // Host-only check of the decode kernel's stream-K partition (csrc/decode_partition.h),
 // built with g++ by tests/test_partition_cpu.py.  For a sweep of (N, K, #SMs) it walks
 // every CTA's range exactly as decode_kernel does (DcSteps, the "whole group" test, the
-// partial slot) and checks what decode_kernel's split-group reduction relies on:
+// partial slot) and checks what decode_kernel and decode_combine_kernel rely on:
 //   * the CTA ranges tile the (group, chunk) units, each unit exactly once, in steps of
 //     at most kDcStep chunks that never cross a group or range boundary;
 //   * first_cta / last_cta (closed forms) equal the brute-force definitions;
 //   * a group inside one CTA is written once to y and no partial is written for it;
 //   * a split group gets one partial from each of CTAs first..last, in distinct slots
-//     below 2 * ctas, at exactly the slots the reduction reads (piece_slot), and a CTA
-//     holds pieces of at most two split groups;
-//   * the reduction slices of a split group's CTAs tile its fragments exactly once;
+//     below 2 * ctas, at exactly the slots the combine kernel reads;
 //   * the split flag and the workspace size agree with the partials written;
 //   * the tensor-copy coordinates the producer issues per step (decode_kernel's
 //     issue_weights and activation copy) start inside the tensors, and every innermost
@@ -108,7 +106,7 @@ static void check_shape(int N, int K, int sms) {
     for (int c = 0; c < p.ctas; ++c) {
         DcSteps st;
         st.start(p.c0(c), p.c0(c + 1), KC);
-        int gkc0 = st.kc, npend = 0;
+        int gkc0 = st.kc;
         while (st.more()) {
             const int nk = st.nk(KC);
             CHECK(nk >= 1 && nk <= kDcStep && st.kc + nk <= KC && st.pos + nk <= st.end, "step of %d chunks", nk);
@@ -132,8 +130,6 @@ static void check_shape(int N, int K, int sms) {
                     slot_owner[s] = c;
                     writer_cta[g].push_back(c);
                     writer_slot[g].push_back(s);
-                    ++npend;
-                    CHECK(npend <= 2, "CTA %d holds pieces of %d split groups", c, npend);
                 }
                 gkc0 = 0;
             }
@@ -153,25 +149,18 @@ static void check_shape(int N, int K, int sms) {
         CHECK(direct[g] == 0, "split group %d written directly", g);
         CHECK((int)writer_cta[g].size() == cl - cf + 1, "split group %d: %d partials for CTAs %d..%d", g,
               (int)writer_cta[g].size(), cf, cl);
-        const int pieces = cl - cf + 1;
-        for (int i = 0; i < pieces; ++i) {
+        for (int i = 0; i < (int)writer_cta[g].size(); ++i) {
             const int c = cf + i;
-            // the reduction reads the i-th piece at piece_slot(g, i)
-            CHECK(writer_cta[g][i] == c && writer_slot[g][i] == p.piece_slot(g, i),
-                  "group %d: partial %d from CTA %d in slot %d, the reduction reads CTA %d slot %d", g, i,
-                  writer_cta[g][i], writer_slot[g][i], c, p.piece_slot(g, i));
-        }
-        for (int F : {kDcFrag4 / 2, kDcFrag4}) {   // fragments per partial for 8 and 16 token rows
-            CHECK(p.slice_lo(0, pieces, F) == 0 && p.slice_lo(pieces, pieces, F) == F, "slices of group %d", g);
-            for (int i = 0; i < pieces; ++i)
-                CHECK(p.slice_lo(i, pieces, F) <= p.slice_lo(i + 1, pieces, F), "slice %d of group %d", i, g);
+            // decode_combine_kernel reads slot(cf, g) for the first CTA and 2c for the others
+            const int read_slot = c == cf ? p.slot(cf, g) : 2 * c;
+            CHECK(writer_cta[g][i] == c && writer_slot[g][i] == read_slot,
+                  "group %d: partial %d from CTA %d in slot %d, combine reads CTA %d slot %d", g, i,
+                  writer_cta[g][i], writer_slot[g][i], c, read_slot);
         }
     }
     CHECK(any_split == p.split, "split flag %d, walk found %d", (int)p.split, (int)any_split);
-    const size_t words = ((size_t)p.groups * 4 + 255) / 256 * 256;
-    const size_t need = any_split ? words + (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
+    const size_t need = any_split ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
     CHECK(dc_workspace_bytes(p) == need, "workspace bytes");
-    CHECK(dc_words_bytes(p) % 256 == 0 && dc_words_bytes(p) >= (size_t)p.groups * 4, "arrival words");
 }
 
 int main() {

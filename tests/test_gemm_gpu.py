@@ -334,11 +334,9 @@ def test_query_route():
     from w4a16_opt import query_route
     r = query_route(1, 4096, 4096, 32)
     assert r["kernel"] == "decode" and r["grid"] == torch.cuda.get_device_properties(0).multi_processor_count
-    # 16 groups over 148 CTAs: split groups, reduced inside the one launch
-    assert r["workspace_bytes"] > 0 and r["launches"] == 1
+    assert r["workspace_bytes"] > 0 and r["launches"] == 2   # 16 groups over 148 CTAs: split
     sms = torch.cuda.get_device_properties(0).multi_processor_count
-    r = query_route(1, 256 * sms, 64, 1)   # one whole 256-column group per CTA: no workspace
-    assert r["launches"] == 1 and r["workspace_bytes"] == 0
+    assert query_route(1, 256 * sms, 64, 1)["launches"] == 1   # one whole 256-column group per CTA
     r = query_route(3, 4112, 4160, 65)
     assert r["kernel"] == "decode"
     r = query_route(2048, 14336, 4096, 32)
@@ -376,21 +374,17 @@ def test_c_abi_direct_call(M):
 
 
 def test_shared_workspace_across_shapes():
-    """One workspace serves calls of different shapes in any order (decode stream-K partials):
-    only the arrival words at its head must start at zero, and every call leaves them there."""
+    """One workspace serves calls of different shapes in any order (decode stream-K partials)."""
     from w4a16_opt import make_workspace, w4a16_gemm_out, workspace_bytes
     shapes = [(1, 4096, 4096), (16, 14336, 4096), (3, 1024, 4096), (8, 28672, 4096), (1, 256, 2048), (5, 4096, 14336)]
     ws = make_workspace(max(workspace_bytes(M, N, K, K // 128) for M, N, K in shapes))
-    words = (max(-(-N // 256) for _, N, _ in shapes) * 4 + 255) // 256 * 256   # one word per 256 columns
-    ws[words:].fill_(0xFF)   # NaN bit patterns: a call must write every partial byte it reads
+    ws.fill_(0xFF)   # NaN bit patterns: a call must write every workspace byte it reads
     for rep in range(2):
         for i, (M, N, K) in enumerate(shapes):
             x, q, s, Wp = make_workload(M, N, K, 128, seed=40 + i)
             y = torch.empty(M, N, dtype=torch.half, device="cuda")
             w4a16_gemm_out(Wp, x, s, y, workspace=ws)
             assert_close(y, ref_gemm(x, q, s, 128))
-            torch.cuda.synchronize()
-            assert int((ws[:words].view(torch.int32) & 0x7FFFFFFF).count_nonzero()) == 0, "arrival counts left set"
 
 
 @pytest.mark.parametrize("M,N,K,G", [(1, 4096, 4096, 128), (16, 14336, 4096, 64), (4, 1024, 4096, 128),

@@ -3,7 +3,7 @@
 Memory safety of the stores is checked directly: y is a window inside a larger buffer
 filled with a canary byte pattern.  The guard bands before and after the window must keep
 the pattern, and every element inside it must be written: the window must equal a
-fresh-output call bit for bit.  Cases: decode with split groups (reduced inside the kernel),
+fresh-output call bit for bit.  Cases: decode with split groups (combine kernel),
 with whole groups, with N and K tails; prefill with M and N tails; fp16 and fp32 outputs.
 """
 import pytest

@@ -3,7 +3,7 @@
 ``partition_check.cpp`` includes the partition header the kernels are built from
 (csrc/decode_partition.h) and walks every CTA's range the way decode_kernel does, for
 some 5800 (N, K, #SMs) cases: unit coverage, the first/last-CTA closed forms, direct
-writes versus partial slots, and the slots and slices the split-group reduction reads.  It plays the
+writes versus partial slots, and the slots decode_combine_kernel reads.  It plays the
 role the reference's numpy emulation of its kernel's data flow plays
 (akshay919191/W4A16-GEMM tests/layout.py) for this kernel's work split.
 """

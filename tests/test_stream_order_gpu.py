@@ -19,8 +19,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 PKG = os.path.join(ROOT, "w4a16-gemm_b200")
 
-# decode with column groups split across CTAs (reduced inside the kernel), decode with whole
-# groups per CTA, prefill; G = 64 and 128
+# decode with column groups split across CTAs (+ combine kernel), decode with whole groups
+# per CTA (one launch), prefill; G = 64 and 128
 CASES = [(1, 4096, 4096, 128), (16, 1024, 4096, 64), (4, 256 * 148, 64, 64), (300, 1024, 2048, 64)]
 
 SCRIPT = r"""
@@ -69,4 +69,4 @@ def test_debug_route_trace(cuda_device, tmp_path):
     lines = [ln for ln in err.splitlines() if ln.startswith("w4a16 ")]
     assert [ln.split()[1] for ln in lines] == ["decode", "decode", "decode", "prefill"]
     assert lines[0].startswith("w4a16 decode G=128 M=1 N=4096 K=4096 ")
-    assert all(ln.endswith("launches=1") for ln in lines[:3])
+    assert lines[2].endswith("launches=1") and lines[0].endswith("launches=2")

@@ -37,8 +37,10 @@ def test_noalloc_matches_workspace_entry(M, N, K, uses_scratch, cuda_device):
     stream = torch.cuda.current_stream().cuda_stream
     nbytes = ctypes.c_uint64(0)
     capi.check(lib.w4a16_workspace_bytes(M, N, K, K // G, -1, ctypes.byref(nbytes)), lib)
+    # the decode scratch is 2 partial slots of 16 KB per CTA: 4.6 MiB on 148 SMs, inside the
+    # 6 MiB array whatever the shape (the array's size covers GPUs of up to 192 SMs)
     assert (nbytes.value > 0) == uses_scratch and nbytes.value <= 6 << 20
-    ws = torch.zeros(max(256, nbytes.value), dtype=torch.uint8, device="cuda")
+    ws = torch.empty(max(256, nbytes.value), dtype=torch.uint8, device="cuda")
     for rep in range(2):   # the built-in scratch is reused by consecutive calls
         x, q, s, Wp = make_workload(M, N, K, G, seed=100 * rep + M + N)
         y_ref = torch.empty(M, N, dtype=torch.half, device="cuda")
@@ -47,27 +49,6 @@ def test_noalloc_matches_workspace_entry(M, N, K, uses_scratch, cuda_device):
         capi.check(_call_noalloc(lib, Wp, x, s, y, M, N, K, G, stream), lib)
         torch.cuda.synchronize()
         assert_close(y, y_ref.float().cpu().numpy())
-
-
-def test_noalloc_rejects_a_need_beyond_the_array(cuda_device):
-    """A call whose scratch need exceeds the built-in array fails with W4A16_ERR_WORKSPACE
-    and launches nothing.  The operands are real allocations of the stated sizes (6.4 GB of
-    packed weights), so the call would be a valid GEMM even if it went ahead."""
-    from w4a16_opt import capi
-    lib = capi.load()
-    M, N, K, G = 1, 96 << 20, 128, 64      # 393,216 column groups: their arrival words overflow it
-    nbytes = ctypes.c_uint64(0)
-    capi.check(lib.w4a16_workspace_bytes(M, N, K, K // G, -1, ctypes.byref(nbytes)), lib)
-    assert nbytes.value > 6 << 20
-    Wp = torch.empty(N * K // 8, dtype=torch.int32, device="cuda")
-    x = torch.zeros(M, K, dtype=torch.half, device="cuda")
-    s = torch.zeros(K // G, N, dtype=torch.half, device="cuda")
-    y = torch.empty(M, N, dtype=torch.half, device="cuda")
-    st = lib.w4a16_gemm_noalloc(Wp.data_ptr(), x.data_ptr(), s.data_ptr(), y.data_ptr(), M, N, K, K // G,
-                                Wp.numel(), -1, 0, ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
-    assert st == 16 and "built-in scratch holds" in capi.last_error(lib)
-    del Wp, x, s, y
-    torch.cuda.empty_cache()
 
 
 def test_noalloc_validates_like_gemm(cuda_device):

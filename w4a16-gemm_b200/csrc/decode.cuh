@@ -22,13 +22,10 @@
 //     13-instruction dequant feeds mma.sync directly (weights = A, the <= 16
 //     tokens = the n8 side); one activation fragment serves both blocks.
 //   * A CTA's columns are complete in registers when it leaves a group: a group
-//     covered by one CTA is written to y directly.  A group split across CTAs leaves
-//     one fp32 partial per CTA in the caller's workspace (float4 fragments in register
-//     order, so every store and load is a coalesced 16-byte access).  At the end of its
-//     range each CTA arrives on the group's sense-reversing arrival word; once all of
-//     the group's CTAs have arrived, each sums its own slice of the group's outputs over
-//     every partial in CTA order and writes it to y -- one launch per GEMM, a result
-//     that does not depend on arrival order, no atomics on data.
+//     covered by one CTA is written to y directly; a group split across CTAs
+//     leaves one fp32 partial per CTA in the caller's workspace, and
+//     decode_combine_kernel (launched behind with programmatic dependent launch)
+//     sums them in CTA order -- deterministic, no atomics, no counters.
 //   * Programmatic dependent launch: dependents may launch as soon as every CTA has
 //     started.  By default nothing is read from global memory before
 //     griddepcontrol.wait, so the GEMM is ordered after whatever the previous kernel
@@ -58,7 +55,8 @@ constexpr int kDcWarps = kDcBlocks / kDcBPW;              // consumer warps; war
 constexpr int kDcThreads = (kDcWarps + 1) * 32;           // + the producer warp
 // Ring stages of packed words and scales issued before griddepcontrol.wait when the
 // caller declares its weights resident.  More is not better: a deep early burst from the
-// next GEMM competes with the tail of the previous one for HBM.
+// next GEMM delays the previous GEMM's combine kernel (measured on the decode sweep:
+// 2 stages 2073 GB/s, all 5 stages 1934 GB/s).
 constexpr int kDcPreStages = 2;
 
 template <int MP>
@@ -71,7 +69,7 @@ struct DcCfg {
     static constexpr int SROW = kDcCols * 2;                      // one chunk's scales of the group (512 B)
     static constexpr int S_BYTES = kDcStep * SROW;
     static constexpr int STAGE_BYTES = W_BYTES + X_BYTES + S_BYTES;
-    static constexpr int BAR_BYTES = 2 * ST * 8 + 16;              // full/empty barriers + 2 go flags
+    static constexpr int BAR_BYTES = 2 * ST * 8;
     static constexpr int SMEM = 1024 + ST * STAGE_BYTES + BAR_BYTES;
     static_assert(STAGE_BYTES % 1024 == 0 && X_CHUNK % 1024 == 0, "stage alignment (128-byte swizzle atoms)");
     static_assert(SMEM <= 227 * 1024, "shared memory budget");
@@ -90,56 +88,11 @@ inline DcPartition dc_partition(int N, int K, int num_sms) {
     return cache[key] = dc_cut(N, K, num_sms);
 }
 
-// Sums the fragments [f_lo, f_hi) of split group g's partials over its CTAs in CTA order
-// and writes them to y.  Fragment f of a partial is float4 ((w*kDcBPW + bb)*MT + mt)*32 + lane
-// of consumer warp w: tokens mt*8 + 2*(lane%4) + {0, 1}, columns (w*kDcBPW + bb)*16 + lane/4
-// + {0, 8} of the group.  Called by the 256 consumer threads (index t).
-template <int MT, bool OUT_F32>
-__device__ __forceinline__ void dc_reduce_slice(const DcPartition& part, int g, int f_lo, int f_hi, int t,
-                                                const float* __restrict__ partials, void* __restrict__ yv, int M,
-                                                int N) {
-    constexpr int kBatch = 8;   // partial loads in flight per thread
-    const int cf = part.first_cta(g), pieces = part.last_cta(g) - cf + 1;
-    for (int f = f_lo + t; f < f_hi; f += kDcWarps * 32) {
-        const int lane = f & 31, r = f >> 5, mt = r % MT, wb = r / MT;
-        const int tok0 = mt * 8 + 2 * (lane & 3);
-        const int col0 = g * kDcCols + wb * 16 + (lane >> 2);
-        if (tok0 >= M || col0 >= N) continue;   // padding rows, or blocks past N
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int i0 = 0; i0 < pieces; i0 += kBatch) {
-            float4 v[kBatch];
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i)
-                if (i0 + i < pieces)
-                    v[i] = __ldcg(reinterpret_cast<const float4*>(partials + (size_t)part.piece_slot(g, i0 + i) *
-                                                                                 kDcSlotFloats) + f);
-#pragma unroll
-            for (int i = 0; i < kBatch; ++i)
-                if (i0 + i < pieces) {
-                    sum.x += v[i].x;
-                    sum.y += v[i].y;
-                    sum.z += v[i].z;
-                    sum.w += v[i].w;
-                }
-        }
-        const float out[4] = {sum.x, sum.y, sum.z, sum.w};
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            const int tok = tok0 + (i & 1), col = col0 + 8 * (i >> 1);
-            if (tok < M) {
-                const size_t o = (size_t)tok * N + col;
-                if (OUT_F32) static_cast<float*>(yv)[o] = out[i];
-                else static_cast<__half*>(yv)[o] = __float2half_rn(out[i]);
-            }
-        }
-    }
-}
-
 template <int G, int MP, bool OUT_F32>
 __global__ void __launch_bounds__(kDcThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
               const __grid_constant__ CUtensorMap ts, void* __restrict__ yv, int M, int N, int box_blocks,
-              int box_chunks, DcPartition part, void* __restrict__ workspace, int pre_stages)
+              int box_chunks, DcPartition part, float* __restrict__ partials, int pre_stages)
 {
     using C = DcCfg<MP>;
     constexpr int ST = C::ST;
@@ -257,19 +210,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
 #pragma unroll
                 for (int i = 0; i < 4; ++i) acc[bb][ch][mt][i] = 0.f;
 
-    // split groups this CTA holds a piece of (at most two: its first and its last group)
-    uint32_t* const words = static_cast<uint32_t*>(workspace);
-    float* const partials = reinterpret_cast<float*>(static_cast<uint8_t*>(workspace) + dc_words_bytes(part));
-    int pend0 = 0, pend1 = 0, npend = 0;
-    bool ok = true;
-
     DcSteps st;
     st.start(c0, c1, KC);
     int gkc0 = st.kc;                 // first chunk of the current group inside this CTA
     for (int t = 0; st.more(); ++t) {
         const int nk = st.nk(KC), s = t % ST;
         const int nb0 = st.g * kDcBlocks + warp * BPW;      // this warp's first n16 block
-        if (!__all_sync(0xffffffffu, mbar_wait_sleep(full(s), (t / ST) & 1, kDevTimeoutWeights))) { ok = false; break; }
+        if (!__all_sync(0xffffffffu, mbar_wait_sleep(full(s), (t / ST) & 1, kDevTimeoutWeights))) break;
         if (nb0 < NB) {
             const uint32_t sb = stage(s);
             // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are finite)
@@ -326,84 +273,72 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         const bool whole = st.kc + nk == KC && gkc0 == 0;
         if (st.advance(nk, KC)) {
             // this CTA's part of group g is done: fold the chains (fixed order) and store
+            float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats;
 #pragma unroll
             for (int bb = 0; bb < BPW; ++bb) {
                 const int nb = g * kDcBlocks + warp * BPW + bb;
                 const int colb = (warp * BPW + bb) * 16 + g8;           // column inside the group
 #pragma unroll
-                for (int mt = 0; mt < MT; ++mt) {
-                    float v[4];
+                for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
                     for (int i = 0; i < 4; ++i) {
-                        v[i] = 0.f;
+                        const int tok = mt * 8 + 2 * t4 + (i & 1);
+                        float v = 0.f;
 #pragma unroll
                         for (int ch = 0; ch < CH; ++ch) {
-                            v[i] += acc[bb][ch][mt][i];
+                            v += acc[bb][ch][mt][i];
                             acc[bb][ch][mt][i] = 0.f;
                         }
-                    }
-                    if (whole) {
-#pragma unroll
-                        for (int i = 0; i < 4; ++i) {
-                            const int tok = mt * 8 + 2 * t4 + (i & 1);
+                        if (nb < NB && tok < M) {
                             const int dc = 8 * (i >> 1);
-                            if (nb < NB && tok < M) {
+                            if (whole) {
                                 const size_t o = (size_t)tok * N + g * kDcCols + colb + dc;
-                                if (OUT_F32) static_cast<float*>(yv)[o] = v[i];
-                                else static_cast<__half*>(yv)[o] = __float2half_rn(v[i]);
+                                if (OUT_F32) static_cast<float*>(yv)[o] = v;
+                                else static_cast<__half*>(yv)[o] = __float2half_rn(v);
+                            } else {
+                                __stcg(my + tok * kDcCols + colb + dc, v);
                             }
                         }
-                    } else {
-                        float4* const my = reinterpret_cast<float4*>(partials + (size_t)part.slot(c, g) * kDcSlotFloats);
-                        __stcg(my + ((warp * BPW + bb) * MT + mt) * 32 + lane, make_float4(v[0], v[1], v[2], v[3]));
                     }
-                }
-            }
-            if (!whole) {
-                if (npend == 0) pend0 = g;
-                else pend1 = g;
-                ++npend;
             }
             gkc0 = 0;
         }
     }
+}
 
-    // ------------------------------------------------ split groups: arrive, then reduce this CTA's slice
-    if (npend == 0) return;
-    volatile uint32_t* const s_go = reinterpret_cast<volatile uint32_t*>(smem_raw + (bars - raw) + 2 * ST * 8);
-    // Every consumer warp gets here, also after a timed-out wait (the others then time out
-    // too); the barrier orders every consumer's partial stores before the arrival and makes
-    // the go / no-go decision the same for the whole CTA.
-    if (!bar_red_and_named(1, kDcWarps * 32, ok)) return;
-    if (threadIdx.x == 0) {
-        // Arrival word: bit 31 = phase sense, bits 0..30 = arrivals.  The CTA whose arrival
-        // completes the count starts the next phase (count 0, sense flipped) with a release
-        // store; the others wait for the flip.  The acq_rel atomic releases this CTA's
-        // partial (ordered before it by the barrier) and acquires the earlier arrivals'.
-        const uint32_t old0 = atom_add_acq_rel_gpu(words + pend0, 1u);
-        const uint32_t old1 = npend > 1 ? atom_add_acq_rel_gpu(words + pend1, 1u) : 0u;
-        for (int j = 0; j < npend; ++j) {
-            const int g = j ? pend1 : pend0;
-            const uint32_t old = j ? old1 : old0;
-            const uint32_t pieces = (uint32_t)(part.last_cta(g) - part.first_cta(g) + 1);
-            if ((old & 0x7FFFFFFFu) == pieces - 1) {
-                st_release_gpu(words + g, (old & 0x80000000u) ^ 0x80000000u);
-                s_go[j] = 1;
-            } else {
-                s_go[j] = wait_sense_flip(words + g, old >> 31, kDevTimeoutSplit) ? 1 : 0;
-            }
+// Combines the groups that the stream-K partition split across CTAs: one CTA per
+// (group, token); groups owned by a single CTA were written by decode_kernel already.
+// Launched right behind decode_kernel with programmatic dependent launch, so it is
+// resident early and griddepcontrol.wait releases it once decode_kernel's writes are
+// complete and visible.  Sums the partials in CTA order (deterministic); the loads of
+// 8 partials are issued together so the sum is not one serial chain of L2 trips.
+template <bool OUT_F32>
+__global__ void __launch_bounds__(kDcCols) decode_combine_kernel(void* __restrict__ yv, int N, DcPartition part,
+                                                                 const float* __restrict__ partials) {
+    const int g = blockIdx.x, tok = blockIdx.y;
+    const int cf = part.first_cta(g), cl = part.last_cta(g);
+    pdl_launch_dependents();
+    if (cf == cl) return;
+    pdl_wait();
+    const int col = g * kDcCols + threadIdx.x;
+    if (col >= N) return;
+    // CTA cf may have started in an earlier group (its second slot); every later CTA
+    // of the group starts inside it (its first slot, 2 * cc).
+    const float* const p = partials + tok * kDcCols + threadIdx.x;
+    const int slot_f = part.slot(cf, g);
+    float sum = 0.f;
+    for (int cc = cf; cc <= cl; cc += 8) {
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = cc + i;
+            v[i] = c <= cl ? __ldcg(p + (size_t)(c == cf ? slot_f : 2 * c) * kDcSlotFloats) : 0.f;
         }
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sum += v[i];
     }
-    bar_sync_named(1, kDcWarps * 32);
-    for (int j = 0; j < npend; ++j) {
-        if (!s_go[j]) continue;
-        const int g = j ? pend1 : pend0;
-        const int cf = part.first_cta(g), pieces = part.last_cta(g) - cf + 1;
-        constexpr int F = kDcWarps * kDcBPW * MT * 32;                 // fragments per partial
-        const int i = c - cf;
-        dc_reduce_slice<MT, OUT_F32>(part, g, part.slice_lo(i, pieces, F), part.slice_lo(i + 1, pieces, F),
-                                     threadIdx.x, partials, yv, M, N);
-    }
+    if (OUT_F32) static_cast<float*>(yv)[(size_t)tok * N + col] = sum;
+    else static_cast<__half*>(yv)[(size_t)tok * N + col] = __float2half_rn(sum);
 }
 
 // ------------------------------------------------------------------ host side
@@ -417,7 +352,7 @@ DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
     p.stages = DcCfg<8>::ST;
     p.smem = p.mt == 1 ? DcCfg<8>::SMEM : DcCfg<16>::SMEM;
     p.workspace = dc_workspace_bytes(part);
-    p.launches = 1;
+    p.launches = part.split ? 2 : 1;
     p.valid = part.valid;
     return p;
 }
@@ -441,6 +376,7 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     DeviceInfo dev;
     if ((err = device_info(&dev)) != cudaSuccess) return err;
     const DcPartition part = dc_partition(a.N, a.K, dev.num_sms);
+    float* partials = static_cast<float*>(a.workspace);
     const int box_blocks = std::min(kDcBlocks, a.N / 16);
     const int box_chunks = std::min(kDcStep, a.K / 64);
     CUtensorMap tw, tx, ts;
@@ -456,7 +392,19 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     cfg.attrs = &attr;
     cfg.numAttrs = a.pdl ? 1 : 0;
     const int pre = a.pdl && a.weights_resident ? kDcPreStages : 0;
-    return cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, box_chunks, part, a.workspace, pre);
+    err = cudaLaunchKernelEx(&cfg, kern, tw, tx, ts, a.y, a.M, a.N, box_blocks, box_chunks, part, partials, pre);
+    if (err != cudaSuccess || !part.split) return err;
+    // combine split groups; always launched programmatically dependent on decode_kernel
+    cudaLaunchConfig_t fc = {};
+    fc.gridDim = dim3(part.groups, a.M, 1);
+    fc.blockDim = dim3(kDcCols, 1, 1);
+    fc.stream = a.stream;
+    cudaLaunchAttribute fattr;
+    fattr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    fattr.val.programmaticStreamSerializationAllowed = 1;
+    fc.attrs = &fattr;
+    fc.numAttrs = 1;
+    return cudaLaunchKernelEx(&fc, decode_combine_kernel<F32>, a.y, a.N, part, static_cast<const float*>(partials));
 }
 
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p) {

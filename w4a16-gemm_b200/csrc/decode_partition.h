@@ -1,8 +1,7 @@
 // Stream-K partition of the decode kernel: which (256-column group, 64-wide K chunk)
-// units each CTA processes, how a CTA walks its units, where split groups leave their
-// partial sums and which slice of a split group each of its CTAs reduces.  Plain C++
-// shared by the host planner, decode_kernel and a host-only checker that compiles it
-// without nvcc.
+// units each CTA processes, how a CTA walks its units, and where split groups leave
+// their partial sums.  Plain C++ shared by the host planner, decode_kernel,
+// decode_combine_kernel and a host-only checker that compiles it without nvcc.
 #pragma once
 #include <stddef.h>
 
@@ -18,7 +17,6 @@ constexpr int kDcBlocks = 16;                             // n16 blocks per grou
 constexpr int kDcCols = kDcBlocks * 16;                   // output columns per group
 constexpr int kDcStep = 4;                                // 64-wide K chunks per step
 constexpr int kDcSlotFloats = 16 * kDcCols;               // one partial: 16 tokens x 256 columns
-constexpr int kDcFrag4 = kDcSlotFloats / 4;               // float4 fragments of a partial (8 warps x 2 blocks x 2 x 32 lanes)
 constexpr int kDcMaxCTAs = 1024;
 // Fewest (group, chunk) units a CTA gets: a small GEMM runs on fewer CTAs rather than
 // splitting each column group over dozens of them (its copies are all in flight at once
@@ -50,16 +48,6 @@ struct DcPartition {
     }
     // Workspace slot of CTA c's partial of group g (only for split groups).
     W4A16_HD int slot(int c, int g) const { return 2 * c + (g == c0(c) / kc ? 0 : 1); }
-    // Slot of the partial that the i-th CTA (i = c - first_cta(g)) of split group g wrote:
-    // the first CTA may have started in an earlier group (its second slot); every later CTA
-    // of the group starts inside it (its first slot).
-    W4A16_HD int piece_slot(int g, int i) const {
-        const int cf = first_cta(g);
-        return i == 0 ? slot(cf, g) : 2 * (cf + i);
-    }
-    // The float4 fragments [lo, hi) of group g's partials that its i-th CTA of `pieces`
-    // sums over all pieces (frags = fragments per partial): an even split.
-    W4A16_HD int slice_lo(int i, int pieces, int frags) const { return (int)((long long)i * frags / pieces); }
 };
 
 inline DcPartition dc_cut(int N, int K, int num_sms) {
@@ -77,16 +65,11 @@ inline DcPartition dc_cut(int N, int K, int num_sms) {
     return p;
 }
 
-// Workspace, only when some group is split:
-//   * one 32-bit arrival word per group (bit 31: phase sense, bits 0..30: arrivals), padded
-//     to 256 bytes -- zero before the first call; every call leaves each count at zero;
-//   * 2 fp32 partial slots per CTA (a CTA's range splits at most its first and its last
-//     group); a slot is fully written before it is read, so its contents need no set-up.
-W4A16_HD inline size_t dc_words_bytes(const DcPartition& p) {
-    return ((size_t)p.groups * 4 + 255) / 256 * 256;
-}
+// Workspace: 2 fp32 partial slots per CTA (a CTA's range splits at most its first
+// and its last group), only when some group is split.  Always fully written before
+// it is read; no initial contents are assumed.
 inline size_t dc_workspace_bytes(const DcPartition& p) {
-    return p.split ? dc_words_bytes(p) + (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
+    return p.split ? (size_t)2 * p.ctas * kDcSlotFloats * 4 : 0;
 }
 
 // Walks a CTA's chunk range [pos, end) in steps of <= kDcStep chunks that never

@@ -20,7 +20,7 @@ struct GemmArgs {
     bool pdl;             // launch with programmatic dependent launch enabled
     bool weights_resident;// wp/scales are not written by the kernel launched just before:
                           // the decode producer may fetch them before griddepcontrol.wait
-    void* workspace;      // decode scratch: split-group arrival words (zero between calls) + partials
+    void* workspace;      // decode scratch (split-group partials); no initial contents needed
     size_t workspace_bytes;
 };
 
@@ -58,7 +58,7 @@ struct DecodePlan {
     int stages;       // TMA ring depth
     size_t smem;      // dynamic shared memory bytes
     size_t workspace; // bytes of workspace the launch needs
-    int launches;     // kernels launched per call (1)
+    int launches;     // kernels launched: 1, or 2 when a group is split (combine kernel)
     bool valid;
 };
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);

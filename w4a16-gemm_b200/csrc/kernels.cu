@@ -208,11 +208,10 @@ cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int box_c
 // Scratch for callers that are not allowed to allocate device memory themselves:
 // e.g. a host integration whose device memory budget is fixed at start-up, or a
 // foreign-language binding with no device allocator to hand a workspace from.
-// The decode path's split-group arrival words and partials then live in this array,
-// which the module loader reserves (zero-filled) on every device alongside the
-// kernels; nothing is allocated per call.  Every call leaves the arrival words at
-// zero again, and the partials are written before they are read.  All calls on one
-// device share it.
+// The decode path's split-group partials then live in this array, which the module
+// loader reserves on every device alongside the kernels; nothing is allocated per
+// call.  The kernels write every byte of it they read, so its contents never need to
+// start at zero.  All calls on one device share it.
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
 
 cudaError_t noalloc_scratch(void** ptr, size_t* bytes, cudaStream_t stream) {

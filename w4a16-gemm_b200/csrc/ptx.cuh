@@ -24,7 +24,6 @@ enum DeviceError : int {
     kDevTimeoutActivations = 2,  // decode: activation / scale barrier never completed
     kDevTimeoutPipeline = 4,     // prefill: a producer/consumer barrier never completed
     kDevTimeoutDrain = 5,        // error path: in-flight copies did not land in time
-    kDevTimeoutSplit = 6,        // decode: the other CTAs of a split column group never arrived
 };
 
 // Per-device status word (one definition: this header is included by the single
@@ -141,55 +140,10 @@ __device__ __forceinline__ void prefetch_tmap(const void* tmap) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(tmap) : "memory");
 }
 
-// ------------------------------------------------------------------ inter-CTA signalling (gpu scope)
+// ------------------------------------------------------------------ named barriers
 // Named barrier over `count` threads (a multiple of 32) of this CTA; barrier 0 is __syncthreads.
 __device__ __forceinline__ void bar_sync_named(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
-}
-
-// Named barrier that also ANDs a predicate over the `count` threads: true iff every one
-// passed true.
-__device__ __forceinline__ bool bar_red_and_named(uint32_t id, uint32_t count, bool v) {
-    uint32_t r;
-    asm volatile(
-        "{\n\t.reg .pred p, q;\n\t"
-        "setp.ne.u32 q, %3, 0;\n\t"
-        "bar.red.and.pred p, %1, %2, q;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(r) : "r"(id), "r"(count), "r"((uint32_t)v) : "memory");
-    return r != 0;
-}
-
-// Atomic add with acquire-release semantics at gpu scope; returns the old value.
-__device__ __forceinline__ uint32_t atom_add_acq_rel_gpu(uint32_t* p, uint32_t v) {
-    uint32_t old;
-    asm volatile("atom.add.acq_rel.gpu.global.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
-    return old;
-}
-
-__device__ __forceinline__ void st_release_gpu(uint32_t* p, uint32_t v) {
-    asm volatile("st.release.gpu.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
-}
-
-__device__ __forceinline__ uint32_t ld_acquire_gpu(const uint32_t* p) {
-    uint32_t v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// Bounded wait until bit 31 of *p differs from `sense` (the phase flip of a sense-reversing
-// arrival word).  Returns false (and records `code`) after kWaitLimitNs.
-__device__ __forceinline__ bool wait_sense_flip(const uint32_t* p, uint32_t sense, int code) {
-    if ((ld_acquire_gpu(p) >> 31) != sense) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
-        __nanosleep(64);
-        if ((ld_acquire_gpu(p) >> 31) != sense) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            record_device_error(code);
-            return false;
-        }
-    }
 }
 
 // ------------------------------------------------------------------ PDL

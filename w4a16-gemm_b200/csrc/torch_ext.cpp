@@ -35,13 +35,13 @@ void check_tensors(const torch::Tensor& Wp, const torch::Tensor& x, const torch:
     TORCH_CHECK(Wp.device() == x.device() && scales.device() == x.device(), "all tensors must be on one device");
 }
 
-// Workspace for the stream-K decode path: zero-filled when allocated, after which every
-// call leaves its arrival words at zero, so one buffer serves every call on a stream
-// (calls on one stream never overlap).  Eager calls use one buffer per (device, stream).
-// While a stream is being captured into a CUDA graph, the calls of that capture share a
-// buffer taken from the graph's pool (its zero fill is captured once); a new capture on
-// the stream releases the previous capture's.  Both maps are capped: streams come and go
-// in serving engines, and a released buffer's memory is only reused in stream order.
+// Workspace for the split-K decode path (scratch, no initialisation needed): one buffer
+// serves every call on a stream, since calls on one stream never overlap.  Eager calls
+// use one buffer per (device, stream).  While a stream is being captured into a CUDA
+// graph, the calls of that capture share a buffer taken from the graph's pool; a new
+// capture on the stream releases the previous capture's.  Both maps are capped: streams
+// come and go in serving engines, and a released buffer's memory is only reused in
+// stream order.
 torch::Tensor workspace_for(const torch::Tensor& x, uint64_t bytes, cudaStream_t stream) {
     if (bytes == 0) return torch::Tensor();
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
@@ -59,14 +59,14 @@ torch::Tensor workspace_for(const torch::Tensor& x, uint64_t bytes, cudaStream_t
         if (it != captured.end() && it->second.first == capture_id && (uint64_t)it->second.second.numel() >= bytes)
             return it->second.second;
         if (it == captured.end() && captured.size() >= kMaxEntries) captured.clear();
-        auto ws = torch::zeros({(int64_t)bytes}, opts);
+        auto ws = torch::empty({(int64_t)bytes}, opts);
         captured[key] = {capture_id, ws};
         return ws;
     }
     auto it = eager.find(key);
     if (it != eager.end() && (uint64_t)it->second.numel() >= bytes) return it->second;
     if (it == eager.end() && eager.size() >= kMaxEntries) eager.clear();
-    auto ws = torch::zeros({(int64_t)bytes}, opts);
+    auto ws = torch::empty({(int64_t)bytes}, opts);
     eager[key] = ws;
     return ws;
 }
@@ -106,7 +106,7 @@ torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor sca
 }
 
 // Same GEMM into a caller-provided contiguous y: fp16, or fp32 for row-parallel partial sums.
-// `workspace` (optional): a zero-filled CUDA buffer of >= workspace_bytes(...) bytes that the
+// `workspace` (optional): a CUDA buffer of >= workspace_bytes(...) bytes (scratch) that the
 // caller keeps for calls issued in stream order; otherwise the binding supplies one.
 // `weights_resident`: Wp and scales are not written by the kernel launched just before
 // (W4A16_FLAG_WEIGHTS_RESIDENT).

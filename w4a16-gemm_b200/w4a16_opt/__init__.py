@@ -50,9 +50,9 @@ def w4a16_gemm_out(Wp: torch.Tensor, x: torch.Tensor, scales: torch.Tensor, y: t
                    weights_resident: bool = False) -> torch.Tensor:
     """Same GEMM into a preallocated contiguous ``y`` (fp16, or fp32 for partial sums).
 
-    ``workspace``: optional CUDA buffer from ``make_workspace`` (zero-filled once; calls keep
-    the parts that must be zero at zero) reused by calls issued in stream order.  Without it
-    the binding keeps one per (device, stream), or one per capture under CUDA-graph capture.
+    ``workspace``: optional scratch CUDA buffer (see ``make_workspace``; no initialisation
+    needed) reused by calls issued in stream order.  Without it the binding keeps one per
+    (device, stream), or one per capture under CUDA-graph capture.
 
     ``weights_resident``: the caller declares that ``Wp`` and ``scales`` were not written by
     the kernel launched just before this call on the stream (loaded earlier, copied, or made
@@ -69,7 +69,7 @@ def workspace_bytes(M: int, N: int, K: int, groups: int, variant: int = -1) -> i
 
 
 def make_workspace(nbytes: int, device=None) -> torch.Tensor:
-    """A zero-filled workspace buffer of at least ``nbytes`` bytes (the state calls expect)."""
+    """A workspace buffer of at least ``nbytes`` bytes (zero-filled, though no call needs that)."""
     return torch.zeros(max(256, int(nbytes)), dtype=torch.uint8, device=device or "cuda")
 
 
