@@ -146,6 +146,19 @@ __device__ __forceinline__ void bar_sync_named(uint32_t id, uint32_t count) {
     asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(count) : "memory");
 }
 
+// Named barrier that also ANDs a predicate over the `count` threads: true iff every one
+// passed true.
+__device__ __forceinline__ bool bar_red_and_named(uint32_t id, uint32_t count, bool v) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\t"
+        "setp.ne.u32 q, %3, 0;\n\t"
+        "bar.red.and.pred p, %1, %2, q;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(r) : "r"(id), "r"(count), "r"((uint32_t)v) : "memory");
+    return r != 0;
+}
+
 // ------------------------------------------------------------------ PDL
 __device__ __forceinline__ void pdl_wait() {
     asm volatile("griddepcontrol.wait;" ::: "memory");
@@ -172,6 +185,17 @@ __device__ __forceinline__ uint4 lds128(uint32_t addr) {
     asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];"
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr));
     return v;
+}
+
+__device__ __forceinline__ float4 lds128f(uint32_t addr) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(addr));
+    return v;
+}
+
+__device__ __forceinline__ void sts128(uint32_t addr, float4 v) {
+    asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" :: "r"(addr), "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w)
+                 : "memory");
 }
 
 // D(16x8, f32) += A(16x16, f16, row) * B(16x8, f16, col)
