@@ -95,10 +95,8 @@ typedef struct w4a16_route {
     int32_t kernel;     /* 0 = decode (M <= 16 weight-streaming GEMV), 1 = prefill (tcgen05) */
     int32_t config;     /* prefill tile config 1..4 (token tile 32/64/128/256); 0 for decode */
     int32_t tile_m;     /* tokens per tile (decode: 8 or 16 padded rows) */
-    int32_t tile_n;     /* output channels per tile: decode 16 x the n16 blocks of a batch when each
-                           CTA owns whole columns, 256 for the stream-K kernel; prefill 128 */
-    int32_t split_k;    /* decode: 1 when each CTA owns whole columns over all of K, else the
-                           stream-K work units (256 columns x one 64-wide K chunk); prefill: 1 */
+    int32_t tile_n;     /* output channels per tile (decode 256, prefill 128) */
+    int32_t split_k;    /* decode: stream-K work units (256 columns x one 64-wide K chunk); prefill: 1 */
     int32_t grid;       /* CTAs launched */
     int32_t stages;     /* pipeline depth */
     int32_t smem_bytes; /* dynamic shared memory per CTA */

@@ -25,12 +25,11 @@ def _call_noalloc(lib, Wp, x, s, y, M, N, K, G, stream):
                                   Wp.numel(), -1, 0, ctypes.c_void_p(stream))
 
 
-# decode shapes with few columns and a long K, which take the stream-K kernel (its split
-# column groups use the scratch); a decode shape whose CTAs own whole columns and a prefill
-# shape (no scratch at all)
-@pytest.mark.parametrize("M,N,K,uses_scratch", [(1, 256, 14336, True), (16, 512, 28672, True),
-                                                (5, 1024, 57344, True), (8, 768, 28672, True),
-                                                (4, 4096, 4096, False), (64, 4096, 4096, False)])
+# decode shapes whose column groups are split across CTAs (they use the scratch), and one
+# prefill shape (no scratch at all)
+@pytest.mark.parametrize("M,N,K,uses_scratch", [(1, 4096, 4096, True), (16, 14336, 4096, True),
+                                                (5, 1024, 4096, True), (8, 4096, 14336, True),
+                                                (64, 4096, 4096, False)])
 def test_noalloc_matches_workspace_entry(M, N, K, uses_scratch, cuda_device):
     from w4a16_opt import capi
     lib = capi.load()

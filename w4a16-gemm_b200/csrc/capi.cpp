@@ -204,7 +204,7 @@ w4a16_status w4a16_query_route(int64_t M, int64_t N, int64_t K, int64_t groups, 
         out->kernel = 0;
         out->config = 0;
         out->tile_m = r.dp.mt * 8;
-        out->tile_n = r.dp.tile_n;
+        out->tile_n = 256;
         out->split_k = r.dp.units;
         out->grid = r.dp.ctas;
         out->stages = r.dp.stages;

@@ -343,25 +343,9 @@ __global__ void __launch_bounds__(kDcCols) decode_combine_kernel(void* __restric
 
 // ------------------------------------------------------------------ host side
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
-    DecodePlan p{};
+    (void)G;
+    DecodePlan p;
     const DcPartition part = dc_partition(N, K, dev.num_sms);
-    // Whole columns per CTA (no cross-CTA reduction) unless its load imbalance costs more
-    // than the stream-K kernel's combine.
-    const NsPlan ns = ns_plan(M, N, K, G, dev.num_sms);
-    if (ns.valid && ns_preferred(N, K, dev.num_sms, part.split)) {
-        p.whole_columns = true;
-        p.ns = ns;
-        p.mt = M <= 8 ? 1 : 2;
-        p.ctas = ns.ctas;
-        p.units = 1;
-        p.stages = ns.stages;
-        p.smem = ns.smem;
-        p.workspace = 0;
-        p.launches = 1;
-        p.tile_n = 16 * ns.bmax;
-        p.valid = true;
-        return p;
-    }
     p.mt = M <= 8 ? 1 : 2;
     p.ctas = part.ctas;
     p.units = part.total;
@@ -369,11 +353,13 @@ DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev) {
     p.smem = p.mt == 1 ? DcCfg<8>::SMEM : DcCfg<16>::SMEM;
     p.workspace = dc_workspace_bytes(part);
     p.launches = part.split ? 2 : 1;
-    p.tile_n = kDcCols;
     p.valid = part.valid;
     return p;
 }
 
+size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev) {
+    return dc_workspace_bytes(dc_partition(N, K, dev.num_sms));
+}
 
 // Tensor maps of the decode kernel (kernels.cu): packed words viewed as [NB][KC][128] int32,
 // box {128, box_chunks, box_blocks}; x viewed as [KC][M][64] fp16, box {64, MP, box_chunks}
@@ -422,7 +408,6 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
 }
 
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p) {
-    if (p.whole_columns) return launch_decode_ns(a, p.ns);
     const bool f32 = a.out_f32;
     if (a.G == 64) {
         if (p.mt == 1) return f32 ? launch_decode_t<64, 8, true>(a, p) : launch_decode_t<64, 8, false>(a, p);

@@ -5,7 +5,6 @@
 #include <stdint.h>
 
 #include "../../include/w4a16.h"
-#include "decode_ns_plan.h"
 
 namespace w4a16 {
 
@@ -53,21 +52,18 @@ cudaError_t noalloc_scratch(void** ptr, size_t* bytes, cudaStream_t stream);
 
 // ---------------------------------------------------------------- decode (M <= 16)
 struct DecodePlan {
-    bool whole_columns; // decode_ns_kernel (CTAs own whole columns) instead of the stream-K kernel
-    NsPlan ns;          // its plan (when whole_columns)
     int mt;           // 8-token tiles (1: M <= 8, 2: M <= 16)
     int ctas;         // persistent CTAs (one per SM)
-    int units;        // stream-K work units (256 columns x one 64-wide K chunk each); 1 for whole columns
+    int units;        // stream-K work units (256 columns x one 64-wide K chunk each)
     int stages;       // TMA ring depth
     size_t smem;      // dynamic shared memory bytes
     size_t workspace; // bytes of workspace the launch needs
     int launches;     // kernels launched: 1, or 2 when a group is split (combine kernel)
-    int tile_n;       // output columns per tile: 256 (a stream-K group) or 16 x the blocks of a batch
     bool valid;
 };
 DecodePlan plan_decode(int M, int N, int K, int G, const DeviceInfo& dev);
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p);
-cudaError_t launch_decode_ns(const GemmArgs& a, const NsPlan& p);
+size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev);
 
 // ---------------------------------------------------------------- prefill (any M)
 struct PrefillPlan {

@@ -14,7 +14,6 @@
 #include "internal.h"
 #include "ptx.cuh"
 #include "decode.cuh"
-#include "decode_ns.cuh"
 #include "prefill.cuh"
 #include "dequant_kernel.cuh"
 #include "format_kernels.cuh"
@@ -200,38 +199,6 @@ cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int box_c
         k.dims[0] = (uint64_t)a.N; k.dims[1] = (uint64_t)(a.K / a.G);
         k.strides[0] = (uint64_t)a.N * 2;
         k.box[0] = (uint32_t)(16 * box_blocks); k.box[1] = 1;
-        if ((err = encode_tiled(k, ts)) != cudaSuccess) return err;
-    }
-    return cudaSuccess;
-}
-
-cudaError_t make_decode_ns_tensor_maps(const GemmArgs& a, const NsPlan& p, CUtensorMap* tw, CUtensorMap* tx,
-                                       CUtensorMap* ts) {
-    cudaError_t err;
-    {   // packed words [NB][KC][128] int32, box {128, S, 1}: one block's S chunks, one
-        // contiguous run of S * 512 bytes
-        TmapKey k = tmap_key(a.wp, 3, CU_TENSOR_MAP_DATA_TYPE_INT32, CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
-        k.dims[0] = 128; k.dims[1] = (uint64_t)(a.K / 64); k.dims[2] = (uint64_t)(a.N / 16);
-        k.strides[0] = 512; k.strides[1] = (uint64_t)(a.K / 64) * 512;
-        k.box[0] = 128; k.box[1] = (uint32_t)p.S; k.box[2] = 1;
-        if ((err = encode_tiled(k, tw)) != cudaSuccess) return err;
-    }
-    {   // x [M, K] fp16 viewed as [K/64][M][64], box {64, M, S}: the step's M rows per chunk,
-        // unpadded, 128-byte swizzle (chunks past K read as zeros)
-        TmapKey k = tmap_key(a.x, 3, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_128B,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
-        k.dims[0] = 64; k.dims[1] = (uint64_t)a.M; k.dims[2] = (uint64_t)(a.K / 64);
-        k.strides[0] = (uint64_t)a.K * 2; k.strides[1] = 128;
-        k.box[0] = 64; k.box[1] = (uint32_t)a.M; k.box[2] = (uint32_t)p.S;
-        if ((err = encode_tiled(k, tx)) != cudaSuccess) return err;
-    }
-    {   // scales [K/G, N] fp16, box {16, R}: one block's columns, the step's scale rows
-        TmapKey k = tmap_key(a.scales, 2, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, CU_TENSOR_MAP_SWIZZLE_NONE,
-                             CU_TENSOR_MAP_L2_PROMOTION_L2_128B);
-        k.dims[0] = (uint64_t)a.N; k.dims[1] = (uint64_t)(a.K / a.G);
-        k.strides[0] = (uint64_t)a.N * 2;
-        k.box[0] = 16; k.box[1] = (uint32_t)p.R;
         if ((err = encode_tiled(k, ts)) != cudaSuccess) return err;
     }
     return cudaSuccess;
