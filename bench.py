@@ -13,9 +13,10 @@ U[0.002, 0.02] fp16), resident in HBM before the timed region.
 
 * value       -- algorithmic bytes (packed weights + scales + x + y) of all GEMMs
                  per second, device-timed (CUDA events around K CUDA-graph replays).
-* e2e         -- the same metric through the public API (w4a16_opt.w4a16_gemm),
+* e2e         -- the same metric through the public API (w4a16_opt.w4a16_gemm_out),
                  eager calls, with each step's activations copied host->device from
-                 pinned memory and its outputs read back device->host.
+                 pinned memory and its outputs read back device->host (copies on a copy
+                 stream, overlapping the neighbouring steps, as a serving loop does).
 * roofline    -- achieved bytes/s of the decode kernel vs the measured HBM copy
                  bandwidth (MEASURED_PEAKS.json), plus the ncu DRAM traffic per launch
                  from profiles/ when a capture of this workload is committed.
@@ -25,10 +26,15 @@ U[0.002, 0.02] fp16), resident in HBM before the timed region.
 * cpu_baseline -- the reference's CPU path (fp16 dequant + fp32 matmul, torch CPU,
                  all host threads) over one pass of the same 16 GEMMs.
 
-With N > 1 (torchrun, one rank per GPU, NCCL) every projection is tensor-parallel
-over the N ranks: q/o and down split K (fp32 all-reduce), k/v and gate/up split N
-(all-gather).  Total work is fixed, so scaling is "strong"; time is the max over
-ranks.  ``--impl reference`` times the CPU reference path alone (rank 0).
+* tp70b       -- BASELINE configs[4] at this N (N = 1 included): Llama-3-70B gate/up
+                 split along N (all-gather) and down split along K (fp32 all-reduce),
+                 M in {1, 16} (GB/s) and M = 4096 (TFLOP/s), strong scaling, with the
+                 collectives' share of the step.
+
+With N > 1 (torchrun, one rank per GPU, NCCL) every rank serves its own decode sweep
+(replicas of an 8B model: weak scaling; `value` is the sum over ranks, time the max
+over ranks), and the tensor-parallel split is measured in tp70b.  ``--impl reference``
+times the CPU reference path alone (rank 0).
 """
 from __future__ import annotations
 
@@ -56,7 +62,6 @@ METRIC = "HBM GB/s at M≤16 & TFLOP/s at M≥128, 1–8 B200, % of roofline"
 DECODE_SHAPES = (("q/o", 4096, 4096), ("k/v", 1024, 4096), ("gate/up", 14336, 4096), ("down", 4096, 14336))
 DECODE_M = (1, 4, 8, 16)
 DECODE_G = 128
-TP_SPLIT = {"q/o": "row", "k/v": "col", "gate/up": "col", "down": "row"}
 PREFILL_M = (128, 512, 2048, 8192)
 PREFILL_SHAPES = ((14336, 4096), (4096, 14336))
 PREFILL_G = (64, 128)
@@ -92,7 +97,7 @@ def bench_config(world):
             "algorithmic_bytes_per_step": sum(alg_bytes(M, N, K, DECODE_G) for _, N, K in DECODE_SHAPES
                                               for M in DECODE_M),
             "l2": "inputs larger than L2: 16 distinct weight copies per step vs 126 MB L2",
-            "parallelism": "single GPU" if world == 1 else f"tp{world} (col: k/v, gate/up; row: q/o, down)"}
+            "parallelism": "single GPU" if world == 1 else f"{world} replicas (a sweep per GPU); tp{world} in tp70b"}
 
 
 def load_peaks():
@@ -252,76 +257,53 @@ def run_ours(args):
     import w4a16_opt
     from w4a16_opt import tp
 
-    # ---- decode sweep units (inputs identical on every rank: same seeds)
+    # ---- decode sweep units.  With N ranks every rank serves its own full sweep (replicas of
+    # an 8B model, which fits one GPU: weak scaling); the tensor-parallel split of the path is
+    # measured on Llama-3-70B shapes below (tp70b).
     units, step_bytes, in_bytes, out_bytes = [], 0, 0, 0
     seed = 1000
     for name, N, K in DECODE_SHAPES:
         for M in DECODE_M:
             x, q, s, Wp = make_inputs(M, N, K, DECODE_G, seed, "cuda")
             seed += 1
-            u = {"name": name, "M": M, "N": N, "K": K, "x": x, "q": q, "s": s, "Wp": Wp}
-            if world == 1:
-                u["y"] = torch.empty(M, N, dtype=torch.float16, device="cuda")
-            elif TP_SPLIT[name] == "col":
-                layer = tp.ColumnParallelW4A16(Wp, s, N, K)
-                u.update(layer=layer, y_local=torch.empty(M, N // world, dtype=torch.float16, device="cuda"),
-                         y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
-                del u["Wp"]
-            else:
-                layer = tp.RowParallelW4A16(Wp, s, N, K)
-                u.update(layer=layer, x_local=layer.x_slice(x),
-                         part=torch.empty(M, N, dtype=torch.float32, device="cuda"),
-                         y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
-                del u["Wp"]
-            units.append(u)
+            units.append({"name": name, "M": M, "N": N, "K": K, "x": x, "q": q, "s": s, "Wp": Wp,
+                          "y": torch.empty(M, N, dtype=torch.float16, device="cuda")})
             step_bytes += alg_bytes(M, N, K, DECODE_G)
             in_bytes += 2 * M * K
             out_bytes += 2 * M * N
     # one workspace shared by every GEMM of the step (they run in stream order)
-    ws = w4a16_opt.make_workspace(max(w4a16_opt.workspace_bytes(u["M"], u["N"] // (world if "y_local" in u else 1),
-                                                                u["K"] // (world if "x_local" in u else 1),
-                                                                (u["K"] // (world if "x_local" in u else 1)) // DECODE_G)
+    ws = w4a16_opt.make_workspace(max(w4a16_opt.workspace_bytes(u["M"], u["N"], u["K"], u["K"] // DECODE_G)
                                       for u in units))
-    for u in units:
-        if "layer" in u:
-            u["layer"].workspace = ws
     torch.cuda.synchronize()
 
     def make_step(resident):
         def step():
             for u in units:
-                if world == 1:
-                    w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws, weights_resident=resident)
-                elif "x_local" in u:
-                    u["layer"].partial(u["x_local"], out=u["part"])
-                    u["layer"].reduce(u["part"], out=u["y"])
-                else:
-                    u["layer"].local(u["x"], out=u["y_local"])
-                    u["layer"].gather(u["y_local"], out=u["y"])
+                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws, weights_resident=resident)
         return step
 
-    # kernels of ours per step: one decode_kernel per GEMM, as the route query reports
-    launches_per_step = 0
-    for u in units:
-        n_loc = u["N"] // (world if "y_local" in u else 1)
-        k_loc = u["K"] // (world if "x_local" in u else 1)
-        launches_per_step += w4a16_opt.query_route(u["M"], n_loc, k_loc, k_loc // DECODE_G)["launches"]
+    # kernels of ours per step: one decode_kernel per GEMM (+ its combine kernel when a column
+    # group is split across CTAs), as the route query reports
+    launches_per_step = sum(w4a16_opt.query_route(u["M"], u["N"], u["K"], u["K"] // DECODE_G)["launches"]
+                            for u in units)
 
     # headline: weights resident (loaded once, as in serving); the GEMMs stream them while
     # the previous GEMM finishes.  The default stream-ordered mode is measured right after.
     with ClockSampler(smi_index(local)) as clocks:
         ms = graph_time_ms(make_step(True), args.steps, args.warmup, world)
     ms_step = ms / args.steps
-    value = step_bytes * args.steps / (ms / 1e3) / 1e9
+    value = world * step_bytes * args.steps / (ms / 1e3) / 1e9
     ms_default = graph_time_ms(make_step(False), args.steps, args.warmup, world)
-    default_mode = {"value": round(step_bytes * args.steps / (ms_default / 1e3) / 1e9, 2), "unit": "GB/s",
+    default_mode = {"value": round(world * step_bytes * args.steps / (ms_default / 1e3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(ms_default / args.steps, 5),
                     "mode": "plain stream order: each GEMM reads its weights only after the previous kernel "
                             "on the stream has completed (w4a16_gemm default)"}
 
-    # ---- e2e through the public API: each step copies its activations in from pinned host
-    # memory (one transfer), makes the 16 calls into one output buffer, reads it back (one
-    # transfer) and synchronises; host wall time
+    # ---- e2e through the public API: every step copies its activations in from pinned host
+    # memory (one transfer), makes the 16 calls into one output buffer and reads it back (one
+    # transfer), as a serving loop does: the copies run on a copy stream and overlap the
+    # neighbouring steps' GEMMs (two buffer sets), and the host waits for each step's result
+    # one step later.  Host wall time.
     e2e, host_us = None, None
     if world == 1:
         x_off, y_off = [0], [0]
@@ -329,31 +311,52 @@ def run_ours(args):
             x_off.append(x_off[-1] + u["x"].numel())
             y_off.append(y_off[-1] + u["M"] * u["N"])
         host_x = torch.cat([u["x"].flatten() for u in units]).cpu().pin_memory()
-        dev_x = torch.empty(x_off[-1], dtype=torch.float16, device="cuda")
-        host_y = torch.empty(y_off[-1], dtype=torch.float16).pin_memory()
-        dev_y = torch.empty(y_off[-1], dtype=torch.float16, device="cuda")
-        views = [(u, dev_x[x_off[i]:x_off[i + 1]].view(u["M"], u["K"]), dev_y[y_off[i]:y_off[i + 1]].view(u["M"], u["N"]))
-                 for i, u in enumerate(units)]
+        dev_x = [torch.empty(x_off[-1], dtype=torch.float16, device="cuda") for _ in range(2)]
+        host_y = [torch.empty(y_off[-1], dtype=torch.float16).pin_memory() for _ in range(2)]
+        dev_y = [torch.empty(y_off[-1], dtype=torch.float16, device="cuda") for _ in range(2)]
+        views = [[(u, dev_x[b][x_off[i]:x_off[i + 1]].view(u["M"], u["K"]),
+                   dev_y[b][y_off[i]:y_off[i + 1]].view(u["M"], u["N"])) for i, u in enumerate(units)]
+                 for b in range(2)]
+        comp, copy = torch.cuda.current_stream(), torch.cuda.Stream()
+        h2d_done = [torch.cuda.Event() for _ in range(2)]
+        comp_done = [torch.cuda.Event() for _ in range(2)]
+        d2h_done = [torch.cuda.Event() for _ in range(2)]
+        for b in range(2):
+            comp_done[b].record(comp)
 
-        def e2e_step():
-            dev_x.copy_(host_x, non_blocking=True)
-            for u, xv, yv in views:
+        def e2e_step(i):
+            b = i % 2
+            copy.wait_event(comp_done[b])             # buffer set b is free (step i - 2 finished)
+            with torch.cuda.stream(copy):
+                dev_x[b].copy_(host_x, non_blocking=True)
+                h2d_done[b].record(copy)
+            comp.wait_event(h2d_done[b])
+            for u, xv, yv in views[b]:
                 w4a16_opt.w4a16_gemm_out(u["Wp"], xv, u["s"], yv, weights_resident=True)
-            host_y.copy_(dev_y, non_blocking=True)
-            torch.cuda.current_stream().synchronize()
+            comp_done[b].record(comp)
+            copy.wait_event(comp_done[b])
+            with torch.cuda.stream(copy):
+                host_y[b].copy_(dev_y[b], non_blocking=True)
+                d2h_done[b].record(copy)
+            if i > 0:
+                d2h_done[(i - 1) % 2].synchronize()  # the previous step's result is on the host
 
         e2e_steps = max(3, min(args.steps, 2000))
-        for _ in range(max(3, min(args.warmup, 50))):
-            e2e_step()
+        for i in range(max(3, min(args.warmup, 50))):
+            e2e_step(i)
+        d2h_done[0].synchronize()
+        d2h_done[1].synchronize()
         t0 = time.perf_counter()
-        for _ in range(e2e_steps):
-            e2e_step()
+        for i in range(e2e_steps):
+            e2e_step(i)
+        d2h_done[(e2e_steps - 1) % 2].synchronize()
         e2e_s = time.perf_counter() - t0
         e2e = {"value": round(step_bytes * e2e_steps / e2e_s / 1e9, 2), "unit": "GB/s",
                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
                "ms_per_step": round(e2e_s * 1e3 / e2e_steps, 4),
-               "api": "w4a16_opt.w4a16_gemm_out(weights_resident=True), eager, current stream; "
-                      "one H2D copy of the step's activations, one D2H copy of its outputs, a sync per step"}
+               "api": "w4a16_opt.w4a16_gemm_out(weights_resident=True), eager, current stream; per step one "
+                      "H2D copy of its activations and one D2H copy of its outputs on a copy stream, "
+                      "overlapping the neighbouring steps' GEMMs; each step's result waited for one step later"}
         # host cost of one eager call (Python + binding + C ABI + launch), GPU work well below it
         u0 = units[0]
         for _ in range(200):
@@ -365,19 +368,19 @@ def run_ours(args):
             w4a16_opt.w4a16_gemm_out(u0["Wp"], u0["x"], u0["s"], u0["y"], weights_resident=True)
         host_us = round((time.perf_counter() - t0) / n_calls * 1e6, 2)
         torch.cuda.synchronize()
-        del host_x, dev_x, host_y, dev_y, views
+        del host_x, dev_x, host_y, dev_y, views, copy
 
     peaks, peak_kind = load_peaks()
     traffic = profile_traffic("decode_sweep_traffic")
-    roofline = {"bound": "hbm", "kernel": "w4a16::decode_kernel", "achieved": round(value, 1),
-                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(value / peaks["hbm_gbs"], 4),
+    roofline = {"bound": "hbm", "kernel": "w4a16::decode_kernel", "achieved": round(value / world, 1),
+                "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": round(value / world / peaks["hbm_gbs"], 4),
                 "peak_source": f"hbm_gbs ({peak_kind})",
                 "traffic": None if traffic is None else traffic.get("decode_kernel_dram_bytes_per_step"),
                 "algorithmic_bytes_per_step": step_bytes,
                 "timing": "CUDA events around the step graph's replays: every GEMM of the step is one "
                           "decode_kernel launch, so this is the kernel time including the gaps between launches"}
     if world > 1:
-        roofline["note"] = "per-rank time includes the NCCL collectives of the TP split"
+        roofline["note"] = "per GPU: every rank streams its own sweep"
 
     # ---- prefill per shape, N = 1: one CUDA graph per (M, N, K, G) over distinct
     # weight copies (>= 256 MB of weights per graph, twice the L2)
@@ -434,6 +437,9 @@ def run_ours(args):
     if world == 1 and rank == 0 and not args.no_gpu_reference:
         gpu_ref = gpu_reference_baseline(units, step_bytes, value, prefill, args)
 
+    # ---- Llama-3-70B tensor-parallel projections over the N ranks (N = 1 included)
+    tp70b = None if args.no_tp else run_tp70b(world, rank, args, peaks, peak_kind)
+
     if world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -446,14 +452,111 @@ def run_ours(args):
     out = {
         "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
-        "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded: x~N(0,1) fp16, q~U{0..15}, scales~U[0.002,0.02] fp16)",
         "config": config, "default_mode": default_mode,
         "e2e": e2e, "host_us_per_call": host_us, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
-        "gpu_reference": gpu_ref, "clocks": clocks.summary(), "gpu_launches": launches_per_step * args.steps,
+        "gpu_reference": gpu_ref, "tp70b": tp70b, "clocks": clocks.summary(),
+        "gpu_launches": launches_per_step * args.steps,
     }
     print(json.dumps(out), flush=True)
     return 0
+
+
+TP70B = (("gate/up", "col", 28672, 8192), ("down", "row", 8192, 28672))
+TP70B_DECODE_M = (1, 16)
+TP70B_PREFILL_M = 4096
+
+
+def run_tp70b(world, rank, args, peaks, peak_kind):
+    """Llama-3-70B gate/up (28672 x 8192, split along N: each rank's
+    columns, then an all-gather of y) and down (8192 x 28672, split along K: each rank's fp32
+    partial, then an all-reduce and one cast), G = 128, at M in {1, 16} (GB/s of the full,
+    unsharded GEMMs) and M = 4096 (TFLOP/s).  Total work is fixed as N grows (strong
+    scaling); times are the max over ranks.  The sharded GEMMs are also timed alone, so the
+    collectives' share of each step is reported."""
+    import w4a16_opt
+    from w4a16_opt import tp
+    G = DECODE_G
+
+    def build(Ms, seed):
+        ops, nbytes, flops = [], 0, 0
+        for M in Ms:
+            for name, kind, N, K in TP70B:
+                x, q, s, Wp = make_inputs(M, N, K, G, seed, "cuda")
+                seed += 1
+                del q
+                op = {"M": M, "kind": kind}
+                if world == 1:
+                    op.update(Wp=Wp, x=x, s=s, y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
+                elif kind == "col":
+                    layer = tp.ColumnParallelW4A16(Wp, s, N, K)
+                    op.update(layer=layer, x=x, y_local=torch.empty(M, N // world, dtype=torch.float16, device="cuda"),
+                              y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
+                else:
+                    layer = tp.RowParallelW4A16(Wp, s, N, K)
+                    op.update(layer=layer, x_local=layer.x_slice(x),
+                              part=torch.empty(M, N, dtype=torch.float32, device="cuda"),
+                              y=torch.empty(M, N, dtype=torch.float16, device="cuda"))
+                if world > 1:
+                    del Wp, s
+                ops.append(op)
+                nbytes += alg_bytes(M, N, K, G)
+                flops += 2 * M * N * K
+        torch.cuda.synchronize()
+        return ops, nbytes, flops
+
+    def full_step(ops):
+        def step():
+            for op in ops:
+                if world == 1:
+                    w4a16_opt.w4a16_gemm_out(op["Wp"], op["x"], op["s"], op["y"], weights_resident=True)
+                elif op["kind"] == "col":
+                    op["layer"].local(op["x"], out=op["y_local"])
+                    op["layer"].gather(op["y_local"], out=op["y"])
+                else:
+                    op["layer"].partial(op["x_local"], out=op["part"])
+                    op["layer"].reduce(op["part"], out=op["y"])
+        return step
+
+    def gemm_step(ops):
+        def step():
+            for op in ops:
+                if world == 1:
+                    w4a16_opt.w4a16_gemm_out(op["Wp"], op["x"], op["s"], op["y"], weights_resident=True)
+                elif op["kind"] == "col":
+                    op["layer"].local(op["x"], out=op["y_local"])
+                else:
+                    op["layer"].partial(op["x_local"], out=op["part"])
+        return step
+
+    out = {"workload": "configs[4]: Llama-3-70B gate/up 28672x8192 (column split + all-gather of y) and down "
+                       "8192x28672 (row split + fp32 all-reduce + cast), G=128",
+           "tp": world, "scaling": "strong",
+           "collectives": "none (one GPU)" if world == 1 else "NCCL all_gather_into_tensor / all_reduce (fp32)"}
+    ops, nbytes, _ = build(TP70B_DECODE_M, 7000)
+    steps = max(20, min(args.steps, 2000))
+    ms = graph_time_ms(full_step(ops), steps, args.warmup, world) / steps
+    gms = graph_time_ms(gemm_step(ops), steps, args.warmup, world) / steps
+    gbs = nbytes / (ms / 1e3) / 1e9
+    out["decode"] = {"M": list(TP70B_DECODE_M), "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5),
+                     "gemm_only_ms": round(gms, 5), "collective_share": round(max(0.0, 1 - gms / ms), 3),
+                     "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+    del ops
+    torch.cuda.empty_cache()
+    if not args.no_prefill:
+        ops, _, flops = build((TP70B_PREFILL_M,), 8000)
+        psteps = 5
+        ms = graph_time_ms(full_step(ops), psteps, 2, world) / psteps
+        gms = graph_time_ms(gemm_step(ops), psteps, 2, world) / psteps
+        tf = flops / (ms / 1e3) / 1e12
+        out["prefill"] = {"M": TP70B_PREFILL_M, "value": round(tf, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+                          "gemm_only_ms": round(gms, 4), "collective_share": round(max(0.0, 1 - gms / ms), 3),
+                          "frac_of_tensor_peak_per_gpu": round(tf / world / peaks["bf16_tflops"], 4),
+                          "peak_source": f"bf16_tflops burst ({peak_kind})"}
+        del ops
+        torch.cuda.empty_cache()
+    return out
 
 
 def gpu_reference_baseline(units, step_bytes, value, prefill, args):
@@ -549,7 +652,7 @@ def run_reference(args):
         " (fp16 dequant + fp32 matmul, torch CPU)"
     out = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(secs * 1e3 / args.steps, 3),
-           "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+           "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16",
            "data": "synthetic (seeded, same inputs as the GPU arm)",
            "config": bench_config(world),
            "cpu_baseline": {"value": round(value, 3), "unit": "GB/s", "cores": threads, "kind": "port",
@@ -569,6 +672,7 @@ def main():
     ap.add_argument("--no-prefill", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gpu-reference", action="store_true")
+    ap.add_argument("--no-tp", action="store_true", help="skip the configs[4] tensor-parallel block")
     args = ap.parse_args()
     if args.impl == "reference":
         args.steps = 16 if args.steps is None else args.steps
