@@ -301,9 +301,9 @@ def run_ours(args):
 
     # ---- e2e through the public API: every step copies its activations in from pinned host
     # memory (one transfer), makes the 16 calls into one output buffer and reads it back (one
-    # transfer), as a serving loop does: the copies run on a copy stream and overlap the
-    # neighbouring steps' GEMMs (two buffer sets), and the host waits for each step's result
-    # one step later.  Host wall time.
+    # transfer), as a serving loop does: the copies run on their own streams (one per
+    # direction) and overlap the neighbouring steps' GEMMs (two buffer sets), and the host
+    # waits for each step's result one step later.  Host wall time.
     e2e, host_us = None, None
     if world == 1:
         x_off, y_off = [0], [0]
@@ -317,27 +317,29 @@ def run_ours(args):
         views = [[(u, dev_x[b][x_off[i]:x_off[i + 1]].view(u["M"], u["K"]),
                    dev_y[b][y_off[i]:y_off[i + 1]].view(u["M"], u["N"])) for i, u in enumerate(units)]
                  for b in range(2)]
-        comp, copy = torch.cuda.current_stream(), torch.cuda.Stream()
+        comp, h2d, d2h = torch.cuda.current_stream(), torch.cuda.Stream(), torch.cuda.Stream()
         h2d_done = [torch.cuda.Event() for _ in range(2)]
         comp_done = [torch.cuda.Event() for _ in range(2)]
         d2h_done = [torch.cuda.Event() for _ in range(2)]
         for b in range(2):
             comp_done[b].record(comp)
+            d2h_done[b].record(comp)
 
         def e2e_step(i):
             b = i % 2
-            copy.wait_event(comp_done[b])             # buffer set b is free (step i - 2 finished)
-            with torch.cuda.stream(copy):
+            h2d.wait_event(comp_done[b])              # buffer set b is free (step i - 2 computed)
+            with torch.cuda.stream(h2d):
                 dev_x[b].copy_(host_x, non_blocking=True)
-                h2d_done[b].record(copy)
+                h2d_done[b].record(h2d)
             comp.wait_event(h2d_done[b])
+            comp.wait_event(d2h_done[b])              # step i - 2's outputs have left dev_y[b]
             for u, xv, yv in views[b]:
                 w4a16_opt.w4a16_gemm_out(u["Wp"], xv, u["s"], yv, weights_resident=True)
             comp_done[b].record(comp)
-            copy.wait_event(comp_done[b])
-            with torch.cuda.stream(copy):
+            d2h.wait_event(comp_done[b])
+            with torch.cuda.stream(d2h):
                 host_y[b].copy_(dev_y[b], non_blocking=True)
-                d2h_done[b].record(copy)
+                d2h_done[b].record(d2h)
             if i > 0:
                 d2h_done[(i - 1) % 2].synchronize()  # the previous step's result is on the host
 
@@ -355,7 +357,7 @@ def run_ours(args):
                "h2d_bytes_per_step": in_bytes, "d2h_bytes_per_step": out_bytes, "steps": e2e_steps,
                "ms_per_step": round(e2e_s * 1e3 / e2e_steps, 4),
                "api": "w4a16_opt.w4a16_gemm_out(weights_resident=True), eager, current stream; per step one "
-                      "H2D copy of its activations and one D2H copy of its outputs on a copy stream, "
+                      "H2D copy of its activations and one D2H copy of its outputs on copy streams, "
                       "overlapping the neighbouring steps' GEMMs; each step's result waited for one step later"}
         # host cost of one eager call (Python + binding + C ABI + launch), GPU work well below it
         u0 = units[0]
@@ -368,7 +370,7 @@ def run_ours(args):
             w4a16_opt.w4a16_gemm_out(u0["Wp"], u0["x"], u0["s"], u0["y"], weights_resident=True)
         host_us = round((time.perf_counter() - t0) / n_calls * 1e6, 2)
         torch.cuda.synchronize()
-        del host_x, dev_x, host_y, dev_y, views, copy
+        del host_x, dev_x, host_y, dev_y, views, h2d, d2h
 
     peaks, peak_kind = load_peaks()
     traffic = profile_traffic("decode_sweep_traffic")
@@ -519,6 +521,15 @@ def run_tp70b(world, rank, args, peaks, peak_kind):
                     op["layer"].reduce(op["part"], out=op["y"])
         return step
 
+    def fused_step(ops):
+        def step():
+            for op in ops:
+                if op["kind"] == "col":
+                    op["y"] = op["layer"].fused(op["x"])
+                else:
+                    op["y"] = op["layer"].fused(op["x_local"])
+        return step
+
     def gemm_step(ops):
         def step():
             for op in ops:
@@ -534,6 +545,24 @@ def run_tp70b(world, rank, args, peaks, peak_kind):
                        "8192x28672 (row split + fp32 all-reduce + cast), G=128",
            "tp": world, "scaling": "strong",
            "collectives": "none (one GPU)" if world == 1 else "NCCL all_gather_into_tensor / all_reduce (fp32)"}
+    # the peer-memory exchange (one buffer per rank, mapped by all; the library's exchange
+    # kernel instead of NCCL), sized for the largest step
+    ex = None
+    if world > 1:
+        Ms = TP70B_DECODE_M + (() if args.no_prefill else (TP70B_PREFILL_M,))
+        src_bytes = max(max(M * (N // world) * 2, M * N * 4) for M in Ms for _, _, N, _ in TP70B)
+        y_bytes = max(M * N * 2 for M in Ms for _, _, N, _ in TP70B)
+        ex = tp.PeerExchange(src_bytes, y_bytes)
+
+    def with_fused(ops, steps, warmup, unit_value):
+        if ex is None:
+            return None
+        for op in ops:
+            op["layer"].exchange = ex
+        fms = graph_time_ms(fused_step(ops), steps, warmup, world) / steps
+        return {"value": round(unit_value(fms), 1), "ms_per_step": round(fms, 5),
+                "exchange": "peer-memory exchange kernel (w4a16_tp_allgather / w4a16_tp_allreduce) over NVLink"}
+
     ops, nbytes, _ = build(TP70B_DECODE_M, 7000)
     steps = max(20, min(args.steps, 2000))
     ms = graph_time_ms(full_step(ops), steps, args.warmup, world) / steps
@@ -541,7 +570,8 @@ def run_tp70b(world, rank, args, peaks, peak_kind):
     gbs = nbytes / (ms / 1e3) / 1e9
     out["decode"] = {"M": list(TP70B_DECODE_M), "value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5),
                      "gemm_only_ms": round(gms, 5), "collective_share": round(max(0.0, 1 - gms / ms), 3),
-                     "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4)}
+                     "frac_of_hbm_per_gpu": round(gbs / world / peaks["hbm_gbs"], 4),
+                     "fused": with_fused(ops, steps, args.warmup, lambda t: nbytes / (t / 1e3) / 1e9)}
     del ops
     torch.cuda.empty_cache()
     if not args.no_prefill:
@@ -553,9 +583,12 @@ def run_tp70b(world, rank, args, peaks, peak_kind):
         out["prefill"] = {"M": TP70B_PREFILL_M, "value": round(tf, 1), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
                           "gemm_only_ms": round(gms, 4), "collective_share": round(max(0.0, 1 - gms / ms), 3),
                           "frac_of_tensor_peak_per_gpu": round(tf / world / peaks["bf16_tflops"], 4),
-                          "peak_source": f"bf16_tflops burst ({peak_kind})"}
+                          "peak_source": f"bf16_tflops burst ({peak_kind})",
+                          "fused": with_fused(ops, psteps, 2, lambda t: flops / (t / 1e3) / 1e12)}
         del ops
         torch.cuda.empty_cache()
+    if ex is not None:
+        ex.close()
     return out
 
 

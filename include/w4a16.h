@@ -12,8 +12,9 @@
  * All pointers are CUDA device pointers; `stream` is a cudaStream_t (NULL =
  * legacy default stream).  Functions return W4A16_OK or an error status; the
  * human-readable reason of the last failure on the calling thread is available
- * from w4a16_last_error().  No function allocates device memory, so GEMM
- * launches may be captured in CUDA graphs.
+ * from w4a16_last_error().  No function allocates device memory except the
+ * set-up call w4a16_peer_alloc, so GEMM and exchange launches may be captured in
+ * CUDA graphs.
  *
  * Workspace: the decode path (M <= 16) may split K across SMs and combine the
  * split partial sums through a caller-provided device workspace of
@@ -71,7 +72,8 @@ typedef enum w4a16_status {
     W4A16_ERR_CUDA = 14,             /* a CUDA runtime / driver call failed */
     W4A16_ERR_DEVICE_TIMEOUT = 15,   /* a kernel's bounded wait ran out (see w4a16_device_status) */
     W4A16_ERR_WORKSPACE = 16,        /* workspace missing, too small or misaligned */
-    W4A16_ERR_FLAGS = 17             /* flags holds bits that are not w4a16_flags values */
+    W4A16_ERR_FLAGS = 17,            /* flags holds bits that are not w4a16_flags values */
+    W4A16_ERR_TP_GROUP = 18          /* a w4a16_tp_group or an exchange's sizes are not usable */
 } w4a16_status;
 
 typedef enum w4a16_flags {
@@ -189,6 +191,56 @@ w4a16_status w4a16_quantize(const void* W, int32_t w_dtype, uint8_t* q, void* sc
  * reference (it quantises, then packs). */
 w4a16_status w4a16_quantize_pack(const void* W, int32_t w_dtype, int32_t* Wp, void* scales, int64_t N, int64_t K,
                                  int64_t group_size, void* stream);
+
+/* ------------------------------------------------------------------------------
+ * Tensor-parallel exchange over peer memory (one process per GPU, one node, GPUs that
+ * can map each other's memory, e.g. over NVLink).  No counterpart in the reference,
+ * which has no distributed code.  Each rank allocates one exchange buffer with
+ * w4a16_peer_alloc, sends its handle to the other ranks (any host channel: e.g.
+ * torch.distributed) and maps theirs with w4a16_peer_open.  The first
+ * W4A16_TP_CTRL_BYTES of every buffer are the exchange's flags; the caller places its
+ * data regions after them (offsets multiples of 16).  Every rank must issue the same
+ * exchanges in the same order (on one stream each).  The kernels only load and store
+ * peer memory directly (no multicast, no bulk copies from peer memory).  Every wait for
+ * a peer is bounded: a peer that never arrives sets the device status (see
+ * w4a16_device_status) and the kernel returns instead of hanging. */
+#define W4A16_TP_MAX_RANKS 8
+#define W4A16_TP_CTRL_BYTES 8192u
+
+typedef struct w4a16_ipc_handle {
+    unsigned char bytes[64];   /* a cudaIpcMemHandle_t */
+} w4a16_ipc_handle;
+
+typedef struct w4a16_tp_group {
+    int32_t rank;                          /* this rank, 0 .. world-1 */
+    int32_t world;                         /* ranks, 1 .. W4A16_TP_MAX_RANKS */
+    void* buf[W4A16_TP_MAX_RANKS];         /* every rank's exchange buffer as mapped here (buf[rank]: own) */
+    uint64_t buf_bytes;                    /* size of each buffer */
+} w4a16_tp_group;
+
+/* Allocates a zero-filled exchange buffer of `bytes` on the current device and its IPC
+ * handle (a set-up call: it allocates). */
+w4a16_status w4a16_peer_alloc(uint64_t bytes, void** ptr, w4a16_ipc_handle* handle);
+/* Maps another process's exchange buffer into this one (current device). */
+w4a16_status w4a16_peer_open(const w4a16_ipc_handle* handle, void** ptr);
+/* Unmaps a buffer mapped by w4a16_peer_open. */
+w4a16_status w4a16_peer_close(void* ptr);
+/* Frees a buffer allocated by w4a16_peer_alloc (after every peer has unmapped it). */
+w4a16_status w4a16_peer_free(void* ptr);
+
+/* Row-parallel reduction: every rank holds an fp32 partial sum [M, N] at byte offset
+ * partial_off of its own buffer.  On return (in stream order) every rank's buffer holds
+ * y = the sum of the ranks' partials, added in rank order, as fp16 [M, N] at y_off.  N %
+ * (4 * world) == 0.  Replaces an NCCL all-reduce of the partials followed by a cast. */
+w4a16_status w4a16_tp_allreduce(const w4a16_tp_group* group, uint64_t partial_off, uint64_t y_off, int64_t M,
+                                int64_t N, void* stream);
+
+/* Column-parallel gather: every rank holds its columns y_r fp16 [M, N / world] at byte
+ * offset src_off of its own buffer.  On return every rank's buffer holds y fp16 [M, N]
+ * at y_off, rank r's columns at [r * N / world, (r + 1) * N / world).  N % (4 * world)
+ * == 0.  Replaces an NCCL all-gather and the copy into y's column order. */
+w4a16_status w4a16_tp_allgather(const w4a16_tp_group* group, uint64_t src_off, uint64_t y_off, int64_t M,
+                                int64_t N, void* stream);
 
 /* Reads the current device's status word, set by a kernel whose bounded wait
  * ran out (0 = none).  Synchronises the device.  reset != 0 clears it. */

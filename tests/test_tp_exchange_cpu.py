@@ -1,0 +1,197 @@
+"""The tensor-parallel exchange (csrc/tp_exchange.cuh) checked on the CPU.
+
+* A thread-per-(rank, CTA) emulation of the exchange kernel's protocol -- ready flags,
+  per-CTA done flags, per-CTA epochs, waits that accept a flag at or past the expected
+  epoch -- over shared arrays that stand in for the ranks' buffers.  Random delays move the
+  threads of different ranks and calls past one another; every call must still produce the
+  rank-order sum (reduce) or the column gather, on every rank.  A rank that stops joining
+  (a stalled peer, injected on the host) must make the others' bounded waits end in an
+  error, not a hang.
+* The C ABI's checks of a group and an exchange's regions, which run before any CUDA call.
+"""
+import ctypes
+import random
+import threading
+import time
+
+import numpy as np
+import pytest
+
+CTAS = 4   # the kernel launches a fixed kTpCtas CTAs; a smaller fixed count keeps the emulation fast
+
+
+class PeerTimeout(Exception):
+    pass
+
+
+class Exchange:
+    """Every rank's buffer: ready[src], done[src][cta], epoch[cta], the source and y regions."""
+
+    def __init__(self, world, M, N, gather, limit_s=2.0):
+        self.world, self.M, self.N, self.gather, self.limit = world, M, N, gather, limit_s
+        self.ready = np.zeros((world, world), np.int64)          # [buffer][src]
+        self.done = np.zeros((world, world, CTAS), np.int64)     # [buffer][src][cta]
+        self.epoch = np.zeros((world, CTAS), np.int64)           # [rank][cta]
+        self.y = np.full((world, M, N), np.nan)
+        self.lock = threading.Lock()
+
+    def wait_at_least(self, get, e):
+        t0 = time.monotonic()
+        while True:
+            with self.lock:
+                if get() >= e:
+                    return
+            if time.monotonic() - t0 > self.limit:
+                raise PeerTimeout()
+            time.sleep(0.0005 * random.random())
+
+    def cta(self, rank, cta, src_regions):
+        """One CTA of the exchange kernel on `rank` (phases A, B, C); src_regions[r] is rank
+        r's source region for this call."""
+        W, M, N = self.world, self.M, self.N
+        e = self.epoch[rank, cta] + 1
+        with self.lock:                                           # A: ready into every buffer
+            for t in range(W):
+                self.ready[t, rank] = max(self.ready[t, rank], e)
+        for src in range(W):
+            self.wait_at_least(lambda src=src: self.ready[rank, src], e)
+        nl = N // W                                               # B: this CTA's share of the rank's columns
+        units = M * (nl // 4)
+        for u in range(units * cta // CTAS, units * (cta + 1) // CTAS):
+            m, c4 = u // (nl // 4), (u % (nl // 4)) * 4
+            cols = slice(rank * nl + c4, rank * nl + c4 + 4)
+            if self.gather:
+                vals = src_regions[rank][m, c4:c4 + 4]
+            else:
+                vals = np.zeros(4, np.float32)
+                for src in range(W):                              # rank order
+                    vals = vals + src_regions[src][m, cols]
+            time.sleep(0.0002 * random.random())
+            for t in range(W):
+                self.y[t, m, cols] = np.float16(vals)
+        with self.lock:                                           # C: done into every buffer
+            for t in range(W):
+                self.done[t, rank, cta] = max(self.done[t, rank, cta], e)
+        for src in range(W):
+            self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
+        self.epoch[rank, cta] = e
+
+
+def run_calls(ex, inputs, stall_rank=None, stall_call=None):
+    """Every rank issues the calls in order, with no host synchronisation between ranks (a
+    fast rank runs ahead); each call's CTAs run as threads.  After each call a rank reads its
+    own y: no peer may write the next call's results into it before this rank announced
+    that call.  Returns results[rank][call], or raises the first error."""
+    results = [[] for _ in range(ex.world)]
+    errors = []
+
+    def rank_main(rank):
+        for i, src in enumerate(inputs):
+            if rank == stall_rank and i == stall_call:
+                return                                            # stops joining: never starts call i
+            threads = [threading.Thread(target=_cta, args=(rank, c, src)) for c in range(CTAS)]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join()
+            if errors:
+                return
+            results[rank].append(ex.y[rank].copy())
+
+    def _cta(rank, c, src):
+        try:
+            ex.cta(rank, c, src)
+        except Exception as exc:                                  # noqa: BLE001
+            errors.append(exc)
+
+    ranks = [threading.Thread(target=rank_main, args=(r,)) for r in range(ex.world)]
+    for t in ranks:
+        t.start()
+    for t in ranks:
+        t.join(timeout=60)
+    assert not any(t.is_alive() for t in ranks), "a rank hung"
+    if errors:
+        raise errors[0]
+    return results
+
+
+@pytest.mark.parametrize("world", [2, 3, 4])
+@pytest.mark.parametrize("gather", [False, True])
+def test_exchange_protocol_results(world, gather):
+    rng = np.random.default_rng(world)
+    M, N = 3, 8 * world
+    inputs = []
+    for _ in range(4):
+        if gather:
+            inputs.append([rng.standard_normal((M, N // world)).astype(np.float16) for _ in range(world)])
+        else:
+            inputs.append([rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)])
+    ex = Exchange(world, M, N, gather)
+    results = run_calls(ex, inputs)
+    assert all(len(r) == len(inputs) for r in results)
+    for i, src in enumerate(inputs):
+        if gather:
+            want = np.concatenate(src, axis=1).astype(np.float16)
+        else:
+            acc = np.zeros((M, N), np.float32)
+            for p in src:                                          # rank order
+                acc = acc + p
+            want = acc.astype(np.float16)
+        for r in range(world):
+            assert np.array_equal(results[r][i].astype(np.float16), want), f"rank {r}, call {i}"
+    assert (ex.epoch == len(inputs)).all()
+
+
+def test_stalled_peer_is_an_error_not_a_hang():
+    world, M, N = 3, 2, 24
+    rng = np.random.default_rng(0)
+    inputs = [[rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)] for _ in range(3)]
+    ex = Exchange(world, M, N, gather=False, limit_s=0.5)
+    t0 = time.monotonic()
+    with pytest.raises(PeerTimeout):
+        run_calls(ex, inputs, stall_rank=2, stall_call=1)
+    assert time.monotonic() - t0 < 30
+
+
+# ------------------------------------------------------------------ the C ABI's host-side checks
+
+def _group(lib_capi, world=2, rank=0, ptrs=(256, 512), nbytes=1 << 20):
+    return lib_capi.TpGroup(rank, world, (ctypes.c_void_p * lib_capi.TP_MAX_RANKS)(*ptrs), nbytes)
+
+
+@pytest.mark.parametrize("kw,msg", [
+    (dict(world=0), "world"),
+    (dict(world=9), "world"),
+    (dict(rank=2), "rank"),
+    (dict(ptrs=(256, 0)), "mapped"),
+    (dict(ptrs=(256, 300)), "256-byte aligned"),
+])
+def test_exchange_rejects_bad_groups(kw, msg):
+    from w4a16_opt import capi
+    lib = capi.load()
+    g = _group(capi, **kw)
+    st = lib.w4a16_tp_allreduce(ctypes.byref(g), capi.TP_CTRL_BYTES, 1 << 19, 2, 64, None)
+    assert st in (18, 1, 9) and msg in capi.last_error(lib)
+
+
+@pytest.mark.parametrize("args,msg", [
+    ((96, 1 << 19, 2, 64), "past the flags"),                        # source inside the flags
+    ((8192, 8200, 2, 64), "multiples of 16"),
+    ((8192, 8192 + 256, 2, 64), "overlap"),
+    ((8192, 1 << 19, 2, 62), "multiple of 4 * world"),
+    ((8192, (1 << 20) - 64, 2, 64), "inside the buffers"),            # y runs past the end
+])
+def test_exchange_rejects_bad_regions(args, msg):
+    from w4a16_opt import capi
+    lib = capi.load()
+    g = _group(capi)
+    st = lib.w4a16_tp_allreduce(ctypes.byref(g), *args, None)
+    assert st != 0 and msg in capi.last_error(lib)
+
+
+def test_peer_alloc_rejects_buffers_smaller_than_the_flags():
+    from w4a16_opt import capi
+    lib = capi.load()
+    p, h = ctypes.c_void_p(), capi.IpcHandle()
+    assert lib.w4a16_peer_alloc(1024, ctypes.byref(p), ctypes.byref(h)) == 18
+    assert "W4A16_TP_CTRL_BYTES" in capi.last_error(lib)

@@ -311,6 +311,103 @@ w4a16_status w4a16_quantize_pack(const void* W, int32_t w_dtype, int32_t* Wp, vo
     return ok();
 }
 
+// ------------------------------------------------------------------ tensor-parallel exchange
+w4a16_status w4a16_peer_alloc(uint64_t bytes, void** ptr, w4a16_ipc_handle* handle) {
+    static_assert(sizeof(w4a16_ipc_handle) == sizeof(cudaIpcMemHandle_t), "IPC handle size");
+    if (!ptr || !handle) return fail(W4A16_ERR_NULL_POINTER, "ptr and handle must be non-null");
+    if (bytes < w4a16::kTpCtrlBytes)
+        return fail(W4A16_ERR_TP_GROUP, "an exchange buffer holds at least W4A16_TP_CTRL_BYTES of flags");
+    void* p = nullptr;
+    cudaError_t err = cudaMalloc(&p, (size_t)bytes);
+    if (err == cudaSuccess) err = cudaMemset(p, 0, (size_t)bytes);   // flags and epochs start at zero
+    cudaIpcMemHandle_t h;
+    if (err == cudaSuccess) err = cudaIpcGetMemHandle(&h, p);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        if (p) cudaFree(p);
+        return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    }
+    std::memcpy(handle->bytes, &h, sizeof(h));
+    *ptr = p;
+    return ok();
+}
+
+w4a16_status w4a16_peer_open(const w4a16_ipc_handle* handle, void** ptr) {
+    if (!ptr || !handle) return fail(W4A16_ERR_NULL_POINTER, "ptr and handle must be non-null");
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle->bytes, sizeof(h));
+    const cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_peer_close(void* ptr) {
+    if (!ptr) return fail(W4A16_ERR_NULL_POINTER, "ptr must be non-null");
+    const cudaError_t err = cudaIpcCloseMemHandle(ptr);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+w4a16_status w4a16_peer_free(void* ptr) {
+    if (!ptr) return fail(W4A16_ERR_NULL_POINTER, "ptr must be non-null");
+    const cudaError_t err = cudaFree(ptr);
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+namespace {
+
+// Checks a group and one exchange's regions: src_bytes at src_off and M*N fp16 at y_off,
+// inside every buffer, past the flags, 16-byte aligned.
+w4a16_status tp_check(const w4a16_tp_group* g, uint64_t src_off, uint64_t src_bytes, uint64_t y_off, int64_t M,
+                      int64_t N, w4a16::TpPtrs* p) {
+    if (!g) return fail(W4A16_ERR_NULL_POINTER, "group must be non-null");
+    if (g->world < 1 || g->world > W4A16_TP_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
+        return fail(W4A16_ERR_TP_GROUP, "group needs 1 <= world <= W4A16_TP_MAX_RANKS and 0 <= rank < world");
+    if (M < 1 || N < 1 || M >= (1LL << 31) || N >= (1LL << 31)) return fail(W4A16_ERR_DIM_RANGE, "dimensions must fit in int32");
+    if (N % (4 * g->world)) return fail(W4A16_ERR_TP_GROUP, "N must be a multiple of 4 * world");
+    const uint64_t y_bytes = (uint64_t)M * (uint64_t)N * 2;
+    if (src_off % 16 || y_off % 16) return fail(W4A16_ERR_ALIGNMENT, "exchange offsets must be multiples of 16");
+    if (src_off < w4a16::kTpCtrlBytes || y_off < w4a16::kTpCtrlBytes || src_off + src_bytes > g->buf_bytes ||
+        y_off + y_bytes > g->buf_bytes)
+        return fail(W4A16_ERR_TP_GROUP, "exchange regions must lie past the flags and inside the buffers");
+    if ((src_off < y_off + y_bytes) && (y_off < src_off + src_bytes))
+        return fail(W4A16_ERR_TP_GROUP, "the source and result regions must not overlap");
+    for (int r = 0; r < g->world; ++r) {
+        if (!g->buf[r]) return fail(W4A16_ERR_NULL_POINTER, "every rank's buffer must be mapped");
+        if (reinterpret_cast<uintptr_t>(g->buf[r]) % 256) return fail(W4A16_ERR_ALIGNMENT, "buffers must be 256-byte aligned");
+        p->buf[r] = static_cast<char*>(g->buf[r]);
+    }
+    for (int r = g->world; r < W4A16_TP_MAX_RANKS; ++r) p->buf[r] = nullptr;
+    return ok();
+}
+
+w4a16_status tp_launch(bool gather, const w4a16_tp_group* g, uint64_t src_off, uint64_t y_off, int64_t M, int64_t N,
+                       void* stream) {
+    w4a16::TpPtrs p;
+    const uint64_t src_bytes = gather ? (uint64_t)M * (uint64_t)(N / (g ? g->world : 1)) * 2 : (uint64_t)M * (uint64_t)N * 4;
+    w4a16_status s = tp_check(g, src_off, src_bytes, y_off, M, N, &p);
+    if (s != W4A16_OK) return s;
+    w4a16::DeviceInfo d;
+    if ((s = check_device(&d)) != W4A16_OK) return s;
+    const cudaError_t err = w4a16::launch_tp_exchange(gather, p, g->rank, g->world, src_off, y_off, (int)M, (int)N,
+                                                      static_cast<cudaStream_t>(stream));
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
+    return ok();
+}
+
+}  // namespace
+
+w4a16_status w4a16_tp_allreduce(const w4a16_tp_group* group, uint64_t partial_off, uint64_t y_off, int64_t M,
+                                int64_t N, void* stream) {
+    return tp_launch(false, group, partial_off, y_off, M, N, stream);
+}
+
+w4a16_status w4a16_tp_allgather(const w4a16_tp_group* group, uint64_t src_off, uint64_t y_off, int64_t M, int64_t N,
+                                void* stream) {
+    return tp_launch(true, group, src_off, y_off, M, N, stream);
+}
+
 w4a16_status w4a16_device_status(int32_t* code, int32_t reset) {
     if (!code) return fail(W4A16_ERR_NULL_POINTER, "code must be non-null");
     int c = 0;
@@ -341,6 +438,7 @@ const char* w4a16_status_string(w4a16_status status) {
         case W4A16_ERR_DEVICE_TIMEOUT: return "W4A16_ERR_DEVICE_TIMEOUT";
         case W4A16_ERR_WORKSPACE: return "W4A16_ERR_WORKSPACE";
         case W4A16_ERR_FLAGS: return "W4A16_ERR_FLAGS";
+        case W4A16_ERR_TP_GROUP: return "W4A16_ERR_TP_GROUP";
     }
     return "W4A16_ERR_UNKNOWN";
 }

@@ -88,6 +88,14 @@ cudaError_t launch_pack(const void* q, void* wp, int N, int K, cudaStream_t stre
 cudaError_t launch_quantize(const void* W, bool w_f16, void* q, void* wp, void* scales, int N, int K, int G,
                             cudaStream_t stream);
 
+// ---------------------------------------------------------------- tensor-parallel exchange
+struct TpPtrs {
+    char* buf[W4A16_TP_MAX_RANKS];   // every rank's exchange buffer as mapped in this process
+};
+constexpr size_t kTpCtrlBytes = W4A16_TP_CTRL_BYTES;
+cudaError_t launch_tp_exchange(bool gather, const TpPtrs& p, int rank, int world, uint64_t src_off, uint64_t y_off,
+                               int M, int N, cudaStream_t stream);
+
 // ---------------------------------------------------------------- debug dequant
 cudaError_t launch_dequant(const void* wp, const void* scales, void* out, int N, int K, int G,
                            cudaStream_t stream);

@@ -17,6 +17,7 @@
 #include "prefill.cuh"
 #include "dequant_kernel.cuh"
 #include "format_kernels.cuh"
+#include "tp_exchange.cuh"
 
 namespace w4a16 {
 

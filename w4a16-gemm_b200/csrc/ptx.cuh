@@ -24,6 +24,7 @@ enum DeviceError : int {
     kDevTimeoutActivations = 2,  // decode: activation / scale barrier never completed
     kDevTimeoutPipeline = 4,     // prefill: a producer/consumer barrier never completed
     kDevTimeoutDrain = 5,        // error path: in-flight copies did not land in time
+    kDevTimeoutPeer = 7,         // tensor-parallel exchange: a peer rank never arrived
 };
 
 // Per-device status word (one definition: this header is included by the single

@@ -22,8 +22,10 @@ STATUS_NAMES = {
     4: "W4A16_ERR_DIM_RANGE", 5: "W4A16_ERR_K_MULTIPLE", 6: "W4A16_ERR_N_MULTIPLE", 7: "W4A16_ERR_GROUPS",
     8: "W4A16_ERR_WP_SIZE", 9: "W4A16_ERR_ALIGNMENT", 10: "W4A16_ERR_GROUP_SIZE",
     11: "W4A16_ERR_DECODE_SHAPE", 12: "W4A16_ERR_OUT_DTYPE", 13: "W4A16_ERR_DEVICE", 14: "W4A16_ERR_CUDA",
-    15: "W4A16_ERR_DEVICE_TIMEOUT", 16: "W4A16_ERR_WORKSPACE", 17: "W4A16_ERR_FLAGS",
+    15: "W4A16_ERR_DEVICE_TIMEOUT", 16: "W4A16_ERR_WORKSPACE", 17: "W4A16_ERR_FLAGS", 18: "W4A16_ERR_TP_GROUP",
 }
+TP_MAX_RANKS = 8
+TP_CTRL_BYTES = 8192
 
 
 class Route(ctypes.Structure):
@@ -33,6 +35,15 @@ class Route(ctypes.Structure):
 
 
 _i64, _i32, _u64, _vp = ctypes.c_int64, ctypes.c_int32, ctypes.c_uint64, ctypes.c_void_p
+
+
+class IpcHandle(ctypes.Structure):
+    _fields_ = [("bytes", ctypes.c_ubyte * 64)]
+
+
+class TpGroup(ctypes.Structure):
+    _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("buf", ctypes.c_void_p * TP_MAX_RANKS),
+                ("buf_bytes", ctypes.c_uint64)]
 
 # name -> (restype, argtypes), one entry per declaration in include/w4a16.h
 EXPORTS = {
@@ -48,6 +59,12 @@ EXPORTS = {
     "w4a16_pack": (_i32, [_vp, _vp, _i64, _i64, _vp]),
     "w4a16_quantize": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _vp]),
     "w4a16_quantize_pack": (_i32, [_vp, _i32, _vp, _vp, _i64, _i64, _i64, _vp]),
+    "w4a16_peer_alloc": (_i32, [_u64, ctypes.POINTER(_vp), ctypes.POINTER(IpcHandle)]),
+    "w4a16_peer_open": (_i32, [ctypes.POINTER(IpcHandle), ctypes.POINTER(_vp)]),
+    "w4a16_peer_close": (_i32, [_vp]),
+    "w4a16_peer_free": (_i32, [_vp]),
+    "w4a16_tp_allreduce": (_i32, [ctypes.POINTER(TpGroup), _u64, _u64, _i64, _i64, _vp]),
+    "w4a16_tp_allgather": (_i32, [ctypes.POINTER(TpGroup), _u64, _u64, _i64, _i64, _vp]),
     "w4a16_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
     "w4a16_status_string": (ctypes.c_char_p, [_i32]),
     "w4a16_last_error": (ctypes.c_char_p, []),

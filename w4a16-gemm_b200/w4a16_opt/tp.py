@@ -11,6 +11,13 @@ The packed format shards without repacking along N and with one slice along K:
   Each rank multiplies its K slice of x into an fp32 partial [M, N]; an fp32
   all-reduce sums the partials and one cast gives fp16 y.
 
+The exchange step is NCCL (all_gather_into_tensor / all_reduce) by default.  Given a
+``PeerExchange`` the layers instead exchange through one buffer per rank that every rank
+maps (CUDA IPC): the row-parallel sums are reduced and the column-parallel outputs
+gathered by the library's own exchange kernel (w4a16_tp_allreduce / w4a16_tp_allgather),
+which loads and stores the peers' buffers directly -- one small launch per exchange, the
+partials summed in rank order, the result written into every rank's buffer.
+
 The reference has no distributed code; this layer follows the sharding the
 north-star configuration asks for (Llama-3-70B gate/up split along N, down
 split along K).  The GEMM itself is always the CUDA kernel; ``gemm_out`` is
@@ -25,6 +32,94 @@ import torch
 import torch.distributed as dist
 
 GemmOut = Callable[[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor], torch.Tensor]
+
+
+class _CudaRegion:
+    """A device-memory range presented through __cuda_array_interface__ (for a zero-copy view)."""
+
+    def __init__(self, ptr, shape, typestr):
+        self.__cuda_array_interface__ = {"shape": tuple(shape), "typestr": typestr, "data": (ptr, False),
+                                         "version": 3, "strides": None}
+
+
+class PeerExchange:
+    """One exchange buffer per rank of ``group``, mapped by every rank (CUDA IPC over NVLink).
+
+    Layout of each buffer: the exchange's flags (``TP_CTRL_BYTES``), then a source region of
+    ``src_bytes`` (this rank's GEMM output: fp32 partials or fp16 columns), then a result
+    region of ``y_bytes`` (fp16 y, written by every rank).  Layers sharing one exchange must
+    be called in the same order on every rank, on one stream each; a result view stays valid
+    until the next exchange.  ``close()`` unmaps and frees (collective).
+    """
+
+    def __init__(self, src_bytes: int, y_bytes: int, group=None):
+        from . import capi
+        import ctypes
+        self._capi, self._ct = capi, ctypes
+        self.lib = capi.load()
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if self.world > capi.TP_MAX_RANKS:
+            raise ValueError(f"at most {capi.TP_MAX_RANKS} ranks")
+        self.src_off = capi.TP_CTRL_BYTES
+        self.y_off = self.src_off + (int(src_bytes) + 255) // 256 * 256
+        self.nbytes = self.y_off + (int(y_bytes) + 255) // 256 * 256
+        own = ctypes.c_void_p()
+        handle = capi.IpcHandle()
+        capi.check(self.lib.w4a16_peer_alloc(self.nbytes, ctypes.byref(own), ctypes.byref(handle)), self.lib)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, bytes(handle.bytes), group=group)
+        self.ptrs = []
+        for r, hb in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(own.value)
+                continue
+            h = capi.IpcHandle()
+            ctypes.memmove(h.bytes, hb, len(hb))
+            p = ctypes.c_void_p()
+            capi.check(self.lib.w4a16_peer_open(ctypes.byref(h), ctypes.byref(p)), self.lib)
+            self.ptrs.append(p.value)
+        self.tp_group = capi.TpGroup(self.rank, self.world,
+                                     (ctypes.c_void_p * capi.TP_MAX_RANKS)(*self.ptrs), self.nbytes)
+        dist.barrier(group=group)   # every rank has mapped every buffer before the first exchange
+
+    def view(self, offset: int, shape, dtype: torch.dtype) -> torch.Tensor:
+        """A tensor over this rank's own buffer at ``offset`` (no copy, no ownership)."""
+        typestr = {torch.float16: "<f2", torch.float32: "<f4"}[dtype]
+        return torch.as_tensor(_CudaRegion(self.ptrs[self.rank] + offset, shape, typestr), device="cuda")
+
+    def src(self, shape, dtype: torch.dtype) -> torch.Tensor:
+        return self.view(self.src_off, shape, dtype)
+
+    def y(self, M: int, N: int) -> torch.Tensor:
+        return self.view(self.y_off, (M, N), torch.float16)
+
+    def allreduce(self, M: int, N: int) -> torch.Tensor:
+        """Every rank's fp32 partial [M, N] (its source region) summed in rank order into
+        every rank's y [M, N] fp16; returns this rank's y."""
+        self._capi.check(self.lib.w4a16_tp_allreduce(self._ct.byref(self.tp_group), self.src_off, self.y_off, M, N,
+                                                     self._ct.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                         self.lib)
+        return self.y(M, N)
+
+    def allgather(self, M: int, N: int) -> torch.Tensor:
+        """Every rank's fp16 columns [M, N / world] (its source region) into every rank's y
+        [M, N], rank r's at columns [r N / world, (r + 1) N / world); returns this rank's y."""
+        self._capi.check(self.lib.w4a16_tp_allgather(self._ct.byref(self.tp_group), self.src_off, self.y_off, M, N,
+                                                     self._ct.c_void_p(torch.cuda.current_stream().cuda_stream)),
+                         self.lib)
+        return self.y(M, N)
+
+    def close(self) -> None:
+        torch.cuda.synchronize()
+        dist.barrier(group=self.group)   # nobody touches a peer's buffer any more
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                self._capi.check(self.lib.w4a16_peer_close(self._ct.c_void_p(p)), self.lib)
+        dist.barrier(group=self.group)   # every peer has unmapped this rank's buffer
+        self._capi.check(self.lib.w4a16_peer_free(self._ct.c_void_p(self.ptrs[self.rank])), self.lib)
+        self.ptrs = []
 
 
 def _default_gemm_out(Wp, x, scales, y, workspace=None):
@@ -68,9 +163,13 @@ def shard_rows(Wp: torch.Tensor, scales: torch.Tensor, N: int, K: int, rank: int
 
 
 class ColumnParallelW4A16:
-    """y = x @ W^T with W split along N over the process group; returns full y [M, N]."""
+    """y = x @ W^T with W split along N over the process group; returns full y [M, N].
 
-    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None):
+    With ``exchange`` (a PeerExchange of this group) ``fused(x)`` writes the local columns into
+    the exchange buffer and gathers them with the library's exchange kernel."""
+
+    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None,
+                 exchange: Optional[PeerExchange] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -80,6 +179,7 @@ class ColumnParallelW4A16:
         self.gemm_out = gemm_out or _default_gemm_out
         self.workspace: Optional[torch.Tensor] = None   # optional GEMM workspace (scratch)
         self._gather_bufs: dict = {}
+        self.exchange = exchange
 
     def local(self, x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         y = out if out is not None else torch.empty(x.shape[0], self.N_local, dtype=torch.float16, device=x.device)
@@ -112,11 +212,22 @@ class ColumnParallelW4A16:
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         return self.gather(self.local(x))
 
+    def fused(self, x: torch.Tensor) -> torch.Tensor:
+        """y [M, N] through the peer exchange: a view of the exchange buffer, valid until
+        the exchange's next call."""
+        M = x.shape[0]
+        self._gemm(x, self.exchange.src((M, self.N_local), torch.float16))
+        return self.exchange.allgather(M, self.N)
+
 
 class RowParallelW4A16:
-    """y = x @ W^T with W split along K; the caller passes this rank's K slice of x."""
+    """y = x @ W^T with W split along K; the caller passes this rank's K slice of x.
 
-    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None):
+    With ``exchange`` (a PeerExchange of this group) ``fused(x_local)`` writes the fp32
+    partial into the exchange buffer and reduces it with the library's exchange kernel."""
+
+    def __init__(self, Wp, scales, N, K, group=None, gemm_out: Optional[GemmOut] = None,
+                 exchange: Optional[PeerExchange] = None):
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -125,6 +236,7 @@ class RowParallelW4A16:
         self.Wp, self.scales = shard_rows(Wp, scales, N, K, self.rank, self.world)
         self.gemm_out = gemm_out or _default_gemm_out
         self.workspace: Optional[torch.Tensor] = None   # optional GEMM workspace (scratch)
+        self.exchange = exchange
 
     def x_slice(self, x: torch.Tensor) -> torch.Tensor:
         return x[:, self.rank * self.K_local:(self.rank + 1) * self.K_local].contiguous()
@@ -146,3 +258,10 @@ class RowParallelW4A16:
 
     def __call__(self, x_local: torch.Tensor) -> torch.Tensor:
         return self.reduce(self.partial(x_local))
+
+    def fused(self, x_local: torch.Tensor) -> torch.Tensor:
+        """y [M, N] fp16 through the peer exchange: a view of the exchange buffer, valid until
+        the exchange's next call."""
+        M = x_local.shape[0]
+        self.partial(x_local, out=self.exchange.src((M, self.N), torch.float32))
+        return self.exchange.allreduce(M, self.N)
