@@ -231,13 +231,13 @@ w4a16_status w4a16_peer_free(void* ptr);
 /* Row-parallel reduction: every rank holds an fp32 partial sum [M, N] at byte offset
  * partial_off of its own buffer.  On return (in stream order) every rank's buffer holds
  * y = the sum of the ranks' partials, added in rank order, as fp16 [M, N] at y_off.  N %
- * (4 * world) == 0.  Replaces an NCCL all-reduce of the partials followed by a cast. */
+ * (8 * world) == 0.  Replaces an NCCL all-reduce of the partials followed by a cast. */
 w4a16_status w4a16_tp_allreduce(const w4a16_tp_group* group, uint64_t partial_off, uint64_t y_off, int64_t M,
                                 int64_t N, void* stream);
 
 /* Column-parallel gather: every rank holds its columns y_r fp16 [M, N / world] at byte
  * offset src_off of its own buffer.  On return every rank's buffer holds y fp16 [M, N]
- * at y_off, rank r's columns at [r * N / world, (r + 1) * N / world).  N % (4 * world)
+ * at y_off, rank r's columns at [r * N / world, (r + 1) * N / world).  N % (8 * world)
  * == 0.  Replaces an NCCL all-gather and the copy into y's column order. */
 w4a16_status w4a16_tp_allgather(const w4a16_tp_group* group, uint64_t src_off, uint64_t y_off, int64_t M,
                                 int64_t N, void* stream);

@@ -56,14 +56,14 @@ class Exchange:
         for src in range(W):
             self.wait_at_least(lambda src=src: self.ready[rank, src], e)
         nl = N // W                                               # B: this CTA's share of the rank's columns
-        units = M * (nl // 4)
+        units = M * (nl // 8)
         for u in range(units * cta // CTAS, units * (cta + 1) // CTAS):
-            m, c4 = u // (nl // 4), (u % (nl // 4)) * 4
-            cols = slice(rank * nl + c4, rank * nl + c4 + 4)
+            m, c8 = u // (nl // 8), (u % (nl // 8)) * 8
+            cols = slice(rank * nl + c8, rank * nl + c8 + 8)
             if self.gather:
-                vals = src_regions[rank][m, c4:c4 + 4]
+                vals = src_regions[rank][m, c8:c8 + 8]
             else:
-                vals = np.zeros(4, np.float32)
+                vals = np.zeros(8, np.float32)
                 for src in range(W):                              # rank order
                     vals = vals + src_regions[src][m, cols]
             time.sleep(0.0002 * random.random())
@@ -119,7 +119,7 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None):
 @pytest.mark.parametrize("gather", [False, True])
 def test_exchange_protocol_results(world, gather):
     rng = np.random.default_rng(world)
-    M, N = 3, 8 * world
+    M, N = 3, 16 * world
     inputs = []
     for _ in range(4):
         if gather:
@@ -143,7 +143,7 @@ def test_exchange_protocol_results(world, gather):
 
 
 def test_stalled_peer_is_an_error_not_a_hang():
-    world, M, N = 3, 2, 24
+    world, M, N = 3, 2, 48
     rng = np.random.default_rng(0)
     inputs = [[rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)] for _ in range(3)]
     ex = Exchange(world, M, N, gather=False, limit_s=0.5)
@@ -178,7 +178,7 @@ def test_exchange_rejects_bad_groups(kw, msg):
     ((96, 1 << 19, 2, 64), "past the flags"),                        # source inside the flags
     ((8192, 8200, 2, 64), "multiples of 16"),
     ((8192, 8192 + 256, 2, 64), "overlap"),
-    ((8192, 1 << 19, 2, 62), "multiple of 4 * world"),
+    ((8192, 1 << 19, 2, 56), "multiple of 8 * world"),
     ((8192, (1 << 20) - 64, 2, 64), "inside the buffers"),            # y runs past the end
 ])
 def test_exchange_rejects_bad_regions(args, msg):

@@ -365,7 +365,7 @@ w4a16_status tp_check(const w4a16_tp_group* g, uint64_t src_off, uint64_t src_by
     if (g->world < 1 || g->world > W4A16_TP_MAX_RANKS || g->rank < 0 || g->rank >= g->world)
         return fail(W4A16_ERR_TP_GROUP, "group needs 1 <= world <= W4A16_TP_MAX_RANKS and 0 <= rank < world");
     if (M < 1 || N < 1 || M >= (1LL << 31) || N >= (1LL << 31)) return fail(W4A16_ERR_DIM_RANGE, "dimensions must fit in int32");
-    if (N % (4 * g->world)) return fail(W4A16_ERR_TP_GROUP, "N must be a multiple of 4 * world");
+    if (N % (8 * g->world)) return fail(W4A16_ERR_TP_GROUP, "N must be a multiple of 8 * world");
     const uint64_t y_bytes = (uint64_t)M * (uint64_t)N * 2;
     if (src_off % 16 || y_off % 16) return fail(W4A16_ERR_ALIGNMENT, "exchange offsets must be multiples of 16");
     if (src_off < w4a16::kTpCtrlBytes || y_off < w4a16::kTpCtrlBytes || src_off + src_bytes > g->buf_bytes ||

@@ -12,8 +12,8 @@
 //                         the same kTpCtas CTAs, of whatever size, so all epochs agree)
 // and the caller's data regions follow.  Call e of an exchange (e = epoch + 1, the same on
 // every rank: all ranks issue the same exchanges in the same order):
-//   A. every CTA writes ready[rank] = e into every buffer, then waits until its own buffer
-//      shows ready[src] >= e for every src;
+//   A. every CTA writes ready[rank] = e into every buffer (after a system-scope fence), then
+//      waits until its own buffer shows ready[src] >= e for every src;
 //   B. reduce: the rank owns columns [rank*N/world, (rank+1)*N/world); its CTAs load those
 //      columns of every rank's fp32 partial, add them in rank order, and store the fp16 sums
 //      into every rank's y.  gather: its CTAs store their own columns into every rank's y;
@@ -39,9 +39,10 @@ namespace w4a16 {
 constexpr int kTpMaxRanks = W4A16_TP_MAX_RANKS;
 // Every exchange launches the same kTpCtas CTAs, whatever its size, so that each CTA's
 // epoch counts every call and the ranks' epochs stay equal.
-constexpr int kTpCtas = 64;
+constexpr int kTpCtas = 32;
 constexpr int kTpMaxCtas = kTpCtas;
-constexpr int kTpThreads = 256;
+constexpr int kTpThreads = 512;
+constexpr int kTpUnroll = 4;   // 8-column units a thread moves per round: their peer loads are in flight together
 constexpr uint32_t kTpReadyOff = 0;
 constexpr uint32_t kTpDoneOff = 1024;
 constexpr uint32_t kTpEpochOff = kTpDoneOff + kTpMaxRanks * kTpMaxCtas * 4;
@@ -64,6 +65,10 @@ __device__ __forceinline__ float4 ld_relaxed_sys_f4(const float4* p) {
     return v;
 }
 
+__device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
+}
+
 __device__ __forceinline__ void fence_acq_rel_sys() {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
@@ -73,7 +78,6 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t e) {
     if ((int32_t)(ld_acquire_sys(p) - e) >= 0) return true;
     const uint64_t t0 = globaltimer_ns();
     while (true) {
-        __nanosleep(32);
         if ((int32_t)(ld_acquire_sys(p) - e) >= 0) return true;
         if (globaltimer_ns() - t0 > kWaitLimitNs) {
             record_device_error(kDevTimeoutPeer);
@@ -86,13 +90,18 @@ __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t e) {
 // GATHER = true: column-parallel gather (src_off: fp16 [M, N/world] in every buffer).
 // Either way every buffer receives fp16 y [M, N] at y_off.
 template <bool GATHER>
-__global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(TpPtrs P, int rank, int world, uint64_t src_off,
+__global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_constant__ TpPtrs P, int rank, int world, uint64_t src_off,
                                                                  uint64_t y_off, int M, int N) {
     __shared__ uint32_t s_e;
     __shared__ int s_ok;
     const int cta = blockIdx.x, tid = threadIdx.x;
     char* const own = P.buf[rank];
     uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff) + cta;
+    // Launched with programmatic dependent launch: the next kernel may start early (it waits
+    // for this one), and this one waits here until the GEMM that wrote the source region has
+    // completed and its writes are visible.
+    pdl_launch_dependents();
+    pdl_wait();
     if (tid == 0) {
         s_e = *epoch + 1u;
         s_ok = 1;
@@ -100,44 +109,82 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(TpPtrs P, int r
     __syncthreads();
     const uint32_t e = s_e;
 
-    // A. ready: this rank's data is in place and its y may be written
-    if (tid < world) st_release_sys(reinterpret_cast<uint32_t*>(P.buf[tid] + kTpReadyOff) + rank, e);
+    // A. ready: this rank's data is in place and its y may be written (one thread; the
+    // release orders the source region, written before this kernel, before the flags)
+    if (tid == 0) {
+        fence_acq_rel_sys();
+        for (int t = 0; t < world; ++t) st_relaxed_sys(reinterpret_cast<uint32_t*>(P.buf[t] + kTpReadyOff) + rank, e);
+    }
     if (tid < world && !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpReadyOff) + tid, e)) s_ok = 0;
     __syncthreads();
     if (!s_ok) return;
 
-    // B. this CTA's share of this rank's columns, 4 at a time
-    const int nl = N / world, q = nl / 4;                          // columns per rank, float4 units per row
+    // B. this CTA's share of this rank's columns, 8 at a time (16-byte peer accesses); a thread
+    // moves kTpUnroll units per round, issuing their loads together
+    const int nl = N / world, q = nl / 8;                          // columns per rank, 8-column units per row
     const long long units = (long long)M * q;
     const long long u0 = units * cta / gridDim.x, u1 = units * (cta + 1) / gridDim.x;
-    for (long long u = u0 + tid; u < u1; u += kTpThreads) {
-        const int m = (int)(u / q), c4 = (int)(u % q) * 4;
-        uint2 h;
-        if (!GATHER) {
-            const size_t at = (size_t)m * N + (size_t)rank * nl + c4;   // element index of the 4 columns
-            float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-            for (int src = 0; src < world; ++src) {                       // rank order
-                const float4 v = ld_relaxed_sys_f4(reinterpret_cast<const float4*>(P.buf[src] + src_off) + at / 4);
-                s.x += v.x;
-                s.y += v.y;
-                s.z += v.z;
-                s.w += v.w;
-            }
-            const __half2 lo = __floats2half2_rn(s.x, s.y), hi = __floats2half2_rn(s.z, s.w);
-            h = make_uint2(*reinterpret_cast<const uint32_t*>(&lo), *reinterpret_cast<const uint32_t*>(&hi));
-            for (int t = 0; t < world; ++t) *reinterpret_cast<uint2*>(P.buf[t] + y_off + at * 2) = h;
-        } else {
-            h = *reinterpret_cast<const uint2*>(own + src_off + ((size_t)m * nl + c4) * 2);
-            const size_t at = (size_t)m * N + (size_t)rank * nl + c4;
-            for (int t = 0; t < world; ++t) *reinterpret_cast<uint2*>(P.buf[t] + y_off + at * 2) = h;
+    for (long long ub = u0 + tid; ub < u1; ub += (long long)kTpThreads * kTpUnroll) {
+        size_t at[kTpUnroll];                                      // element index of a unit's 8 columns in y
+        bool live[kTpUnroll];
+#pragma unroll
+        for (int i = 0; i < kTpUnroll; ++i) {
+            const long long u = ub + (long long)i * kTpThreads;
+            live[i] = u < u1;
+            const int m = live[i] ? (int)(u / q) : 0, c8 = live[i] ? (int)(u % q) * 8 : 0;
+            at[i] = (size_t)m * N + (size_t)rank * nl + c8;
         }
+        uint4 h[kTpUnroll];
+        if (!GATHER) {
+            float4 a[kTpUnroll], b[kTpUnroll];
+#pragma unroll
+            for (int i = 0; i < kTpUnroll; ++i) a[i] = b[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int src = 0; src < world; ++src) {                    // rank order
+                float4 v[kTpUnroll], w[kTpUnroll];
+#pragma unroll
+                for (int i = 0; i < kTpUnroll; ++i)
+                    if (live[i]) {
+                        const float4* p = reinterpret_cast<const float4*>(P.buf[src] + src_off) + at[i] / 4;
+                        v[i] = ld_relaxed_sys_f4(p);
+                        w[i] = ld_relaxed_sys_f4(p + 1);
+                    }
+#pragma unroll
+                for (int i = 0; i < kTpUnroll; ++i)
+                    if (live[i]) {
+                        a[i].x += v[i].x; a[i].y += v[i].y; a[i].z += v[i].z; a[i].w += v[i].w;
+                        b[i].x += w[i].x; b[i].y += w[i].y; b[i].z += w[i].z; b[i].w += w[i].w;
+                    }
+            }
+#pragma unroll
+            for (int i = 0; i < kTpUnroll; ++i) {
+                const __half2 h0 = __floats2half2_rn(a[i].x, a[i].y), h1 = __floats2half2_rn(a[i].z, a[i].w);
+                const __half2 h2 = __floats2half2_rn(b[i].x, b[i].y), h3 = __floats2half2_rn(b[i].z, b[i].w);
+                h[i] = make_uint4(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1),
+                                  *reinterpret_cast<const uint32_t*>(&h2), *reinterpret_cast<const uint32_t*>(&h3));
+            }
+        } else {
+#pragma unroll
+            for (int i = 0; i < kTpUnroll; ++i)
+                if (live[i]) {
+                    const size_t col = at[i] - (size_t)rank * nl;         // m*N + c8
+                    const size_t m = col / (size_t)N, c8 = col % (size_t)N;
+                    h[i] = *reinterpret_cast<const uint4*>(own + src_off + (m * nl + c8) * 2);
+                }
+        }
+#pragma unroll
+        for (int i = 0; i < kTpUnroll; ++i)
+            if (live[i])
+                for (int t = 0; t < world; ++t) *reinterpret_cast<uint4*>(P.buf[t] + y_off + at[i] * 2) = h[i];
     }
     __syncthreads();
 
-    // C. done: this CTA's stores are in every buffer; wait for CTA cta of every rank
-    if (tid < world) {
-        fence_acq_rel_sys();   // the CTA's stores (ordered before by the barrier) before the flag
-        st_release_sys(reinterpret_cast<uint32_t*>(P.buf[tid] + kTpDoneOff) + rank * kTpMaxCtas + cta, e);
+    // C. done: this CTA's stores are in every buffer (one thread: the fence orders the CTA's
+    // stores, made visible to it by the barrier, before the flags); then wait for CTA cta of
+    // every rank
+    if (tid == 0) {
+        fence_acq_rel_sys();
+        for (int t = 0; t < world; ++t)
+            st_relaxed_sys(reinterpret_cast<uint32_t*>(P.buf[t] + kTpDoneOff) + rank * kTpMaxCtas + cta, e);
     }
     if (tid < world && !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpDoneOff) + tid * kTpMaxCtas + cta, e))
         s_ok = 0;
@@ -147,10 +194,17 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(TpPtrs P, int r
 
 cudaError_t launch_tp_exchange(bool gather, const TpPtrs& p, int rank, int world, uint64_t src_off, uint64_t y_off,
                                int M, int N, cudaStream_t stream) {
-    const int b = kTpCtas;
-    if (gather) tp_exchange_kernel<true><<<b, kTpThreads, 0, stream>>>(p, rank, world, src_off, y_off, M, N);
-    else tp_exchange_kernel<false><<<b, kTpThreads, 0, stream>>>(p, rank, world, src_off, y_off, M, N);
-    return cudaGetLastError();
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kTpCtas, 1, 1);
+    cfg.blockDim = dim3(kTpThreads, 1, 1);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr;
+    attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr.val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = &attr;
+    cfg.numAttrs = 1;
+    if (gather) return cudaLaunchKernelEx(&cfg, tp_exchange_kernel<true>, p, rank, world, src_off, y_off, M, N);
+    return cudaLaunchKernelEx(&cfg, tp_exchange_kernel<false>, p, rank, world, src_off, y_off, M, N);
 }
 
 }  // namespace w4a16
