@@ -12,10 +12,14 @@ CTA of the stream-K partition and every step it does three things:
    Bytes the copies do not write hold garbage (random words, NaN scales): lanes that read
    them must not leak into y.
 2. It reads the stage back through the consumer warps' own addressing: `w_lane`,
-   `x_lane0/1` with `ldmatrix.x4`, `s_lane`.  The dequantisation restates the same bit
-   tricks (csrc/dequant.cuh).  The products form `mma.m16n8k16` fragments, accumulated in
-   2 chains per block, and are stored like the kernel's epilogue: straight to y for a
-   whole group, else a partial slot that the combine kernel sums in CTA order.
+   `x_lane0/1` with `ldmatrix.x4`, `s_lane`.  The A fragments restate the same bit tricks
+   (csrc/dequant.cuh): for M <= 8 the unscaled integers q - 8 (`unscaled_word`), whose
+   four products per chunk start from zero and are then scaled per output row by the
+   chunk's scale (the rows of lanes g8 and g8 + 8); for M > 8 the exact fp16 (q - 8) * s
+   (`dequant_word`).  Either way the chunk's result goes to one of 2 accumulator sets per
+   block (alternating by chunk), and the sets are added and stored like the kernel's
+   epilogue: straight to y for a whole group, else a partial slot that the combine kernel
+   sums in CTA order.
 3. It compares the emulated y with the oracle's GEMM.
 
 Hardware facts assumed, from the PTX ISA:
@@ -26,7 +30,9 @@ Hardware facts assumed, from the PTX ISA:
 * the m16n8k16 A/B/C fragment layouts.
 
 Products are accumulated in float64: this checks the index mapping, not the tensor cores'
-rounding.
+rounding.  For M <= 8 the result must equal float64 x @ ((q - 8) * s)^T to 1e-12 (and lie
+within the north-star tolerance of the oracle, whose weights are rounded to fp16 after
+scaling); for M > 8 it must equal the oracle to 1e-5.
 """
 import numpy as np
 import pytest
@@ -81,6 +87,13 @@ def dequant_word(q, s_lo, s_hi):
             half2((q8 & 0x00F000F0) | 0x54005400, 72, s_hi)]
 
 
+def unscaled_word(q):
+    """csrc/dequant.cuh unscaled_word for 32 lanes: a[p] = (lo half, hi half) as fp16 arrays
+    of q - 8."""
+    one = np.ones(32, np.float16)
+    return dequant_word(q, one, one)
+
+
 def build_stage(Wp4, x, scales, g, kc0, nk, N, K, G, MP, rng):
     """The stage's three regions as byte arrays, as the producer's copies leave them."""
     NB, KC = N // 16, K // 64
@@ -131,6 +144,9 @@ def consume(wimg, ximg, simg, box_chunks, nk, MT, acc):
                 s_hi = simg.view(np.uint16)[sa // 2 + 8].view(np.float16) if j < nk else np.zeros(32, np.float16)
                 wa = w * BPW * w_blk + lanes * 16 + j * 512 + bb * w_blk
                 words = np.stack([wimg[a:a + 16].view(np.uint32) for a in wa])       # [32 lanes, 4]
+                srow = np.zeros(16)                       # the chunk's scale of each row of the block
+                srow[g8] = s_lo.astype(np.float64)
+                srow[g8 + 8] = s_hi.astype(np.float64)
                 for mt in range(MT):
                     xa = j * xchunk + mt * 1024
                     b = np.zeros((8, 32, 2), np.float64)      # b[reg][thread][half]
@@ -141,8 +157,9 @@ def consume(wimg, ximg, simg, box_chunks, nk, MT, acc):
                             mat = rows[8 * i:8 * i + 8]                # matrix i: 8 rows x 8 halves
                             b[4 * x4 + i] = np.stack([mat[lanes // 4, 2 * (lanes % 4)],
                                                       mat[lanes // 4, 2 * (lanes % 4) + 1]], 1)
+                    prod = np.zeros((16, 8))
                     for ks in range(4):
-                        a = dequant_word(words[:, ks], s_lo, s_hi)
+                        a = unscaled_word(words[:, ks]) if MT == 1 else dequant_word(words[:, ks], s_lo, s_hi)
                         A = np.zeros((16, 16))
                         for p in range(4):
                             for h in range(2):
@@ -151,7 +168,8 @@ def consume(wimg, ximg, simg, box_chunks, nk, MT, acc):
                         for h in range(2):
                             B[2 * t4 + h, lanes // 4] = b[2 * ks, :, h]
                             B[8 + 2 * t4 + h, lanes // 4] = b[2 * ks + 1, :, h]
-                        acc[w][bb][j % 2][mt] += A @ B
+                        prod += A @ B
+                    acc[w][bb][j % 2][mt] += srow[:, None] * prod if MT == 1 else prod
 
 
 def emulate(Wp, x, scales, N, K, G, sms, seed=0):
@@ -236,10 +254,19 @@ def test_decode_emulation_matches_oracle(M, N, K, G, sms):
     x = rng.standard_normal((M, K)).astype(np.float16)
     Wp = oracle.pack_int4(q)
     y = emulate(Wp, x, scales, N, K, G, sms)
-    ref = oracle.ref_gemm(x, q, scales, G).astype(np.float64)
     assert np.isfinite(y).all(), "an output was not written, or garbage leaked into it"
-    err = np.abs(y - ref).max() / np.abs(ref).max()
-    assert err < 1e-5, err
+    ref = oracle.ref_gemm(x, q, scales, G).astype(np.float64)
+    if M <= 8:
+        # scaled after the products: the exact counterpart is float64 (q - 8) * s, without
+        # the oracle's fp16 rounding of each weight
+        w64 = (q.astype(np.float64) - 8.0) * np.repeat(scales.astype(np.float64).T, G, axis=1)
+        exact = x.astype(np.float64) @ w64.T
+        err = np.abs(y - exact).max() / np.abs(exact).max()
+        assert err < 1e-12, err
+        assert np.linalg.norm(y - ref) / np.linalg.norm(ref) <= 1e-3
+    else:
+        err = np.abs(y - ref).max() / np.abs(ref).max()
+        assert err < 1e-5, err
 
 
 def _header_ints(path, names):
@@ -277,7 +304,14 @@ def test_emulation_index_expressions_match_kernel_source():
         "const uint32_t s_lane = (uint32_t)(C::W_BYTES + C::X_BYTES + warp * BPW * 32 + g8 * 2);",
         "wv[jj][bb] = lds128(wb + (jb + jj) * 512 + bb * w_blk);",
         "const uint32_t xa = sb + (jb + jj) * C::X_CHUNK + mt * 1024;",
+        "unscaled_word(wq, a);",
+        "if (ks == 0) mma_16816_zero(cc[jj][bb][mt], a, b[jj][mt][0], b[jj][mt][1]);",
+        "else mma_16816(cc[jj][bb][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);",
+        "float& d = acc[bb][(jb + jj) % CH][mt][i];",
+        "d = fmaf(i < 2 ? f_lo[bb][jb + jj] : f_hi[bb][jb + jj], cc[jj][bb][mt][i], d);",
+        "dequant_word(wq, h_lo[bb][jb + jj], h_hi[bb][jb + jj], a);",
         "mma_16816(acc[bb][(jb + jj) % CH][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);",
+        "constexpr bool SCALE_AFTER = MT == 1;",
         "const int colb = (warp * BPW + bb) * 16 + g8;",
         "const int tok = mt * 8 + 2 * t4 + (i & 1);",
         "const int dc = 8 * (i >> 1);",

@@ -18,9 +18,12 @@
 //     far better than 512-byte pieces -- the token rows of the step's chunks in
 //     one box (128-byte swizzle, rows >= M zero-filled) and the group's scales.
 //   * Consumer warp w owns n16 blocks 2w and 2w+1 of the group.  The packed word
-//     of each lane is already an m16n8k16 A fragment, so the exact
-//     13-instruction dequant feeds mma.sync directly (weights = A, the <= 16
-//     tokens = the n8 side); one activation fragment serves both blocks.
+//     of each lane is already an m16n8k16 A fragment, fed to mma.sync directly
+//     (weights = A, the <= 16 tokens = the n8 side; one activation fragment serves
+//     both blocks).  For M <= 8 the fragment holds the exact integers q - 8 (9
+//     instructions: 1 shift, 4 LOP3, 4 HSUB2) and each chunk's products are scaled in
+//     fp32 after the tensor core, one FMA per accumulator element; for M > 8 it holds
+//     the exact fp16 (q - 8) * s (13 instructions).
 //   * A CTA's columns are complete in registers when it leaves a group: a group
 //     covered by one CTA is written to y directly; a group split across CTAs
 //     leaves one fp32 partial per CTA in the caller's workspace, and
@@ -186,8 +189,17 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
     }
 
     // ---------------------------------------------------- consumer warp: n16 blocks 2*warp, 2*warp+1 of each group
+    // M <= 8 (MT = 1): per 64-wide chunk and n16 block, a chain of four m16n8k16 products of
+    // the exact integers q - 8 (fp16) with the activations, started from zero, then one fp32
+    // FMA per accumulator element by the chunk's scale (a chunk never straddles two scale
+    // groups: G is a multiple of 64).  9 instructions dequantise a word.
+    // M > 8 (MT = 2): each word is dequantised exactly to fp16 (q - 8) * s, 13 instructions,
+    // and the products accumulate directly.  With twice the tensor-core work per word, the
+    // per-chunk scaling measured slower here (q/o 9.6 against 7.8 us at M = 16).
+    // Either way a block's sums alternate between two accumulator sets, added at the end.
     constexpr int BPW = kDcBPW;
-    constexpr int CH = 2;                                          // accumulator chains per block
+    constexpr int CH = 2;
+    constexpr bool SCALE_AFTER = MT == 1;
     const int g8 = lane >> 2, t4 = lane & 3;
     pdl_wait();   // the workspace and y may still be in use by the previous kernel
 
@@ -219,8 +231,10 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         if (!__all_sync(0xffffffffu, mbar_wait_sleep(full(s), (t / ST) & 1, kDevTimeoutWeights))) break;
         if (nb0 < NB) {
             const uint32_t sb = stage(s);
-            // scales of this step's chunks; chunks beyond nk get scale 0 (their activations are finite)
-            uint32_t s_lo[BPW][kDcStep], s_hi[BPW][kDcStep];
+            // scales of this step's chunks (rows g8 and g8 + 8 of each block), as fp32 or as
+            // broadcast fp16 pairs; chunks beyond nk get scale 0 (their products are finite)
+            float f_lo[BPW][kDcStep], f_hi[BPW][kDcStep];
+            uint32_t h_lo[BPW][kDcStep], h_hi[BPW][kDcStep];
 #pragma unroll
             for (int bb = 0; bb < BPW; ++bb)
 #pragma unroll
@@ -228,8 +242,13 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                     const uint32_t sa = sb + s_lane + bb * 32 + j * C::SROW;
                     const uint16_t lo = lds_u16(sa);
                     const uint16_t hi = lds_u16(sa + 16);
-                    s_lo[bb][j] = j < nk ? bcast_half(lo) : 0u;
-                    s_hi[bb][j] = j < nk ? bcast_half(hi) : 0u;
+                    if (SCALE_AFTER) {
+                        f_lo[bb][j] = j < nk ? __half2float(__ushort_as_half(lo)) : 0.f;
+                        f_hi[bb][j] = j < nk ? __half2float(__ushort_as_half(hi)) : 0.f;
+                    } else {
+                        h_lo[bb][j] = j < nk ? bcast_half(lo) : 0u;
+                        h_hi[bb][j] = j < nk ? bcast_half(hi) : 0u;
+                    }
                 }
             const uint32_t wb = sb + w_lane;
             constexpr int JB = MT == 1 ? 4 : 2;                // chunks whose operands are loaded together
@@ -248,22 +267,54 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
                         ldmatrix_x4(*reinterpret_cast<uint32_t(*)[4]>(&b[jj][mt][4]), xa + x_lane1);
                     }
                 }
-                // No per-chunk guard: the unconditional body lets the accumulator chains interleave.
-                // The activation fragments of a chunk serve both blocks.
+                // No per-chunk guard: the unconditional body lets the chains interleave.  The
+                // activation fragments of a chunk serve both blocks.
+                if constexpr (SCALE_AFTER) {
+                    float cc[JB][BPW][MT][4];
 #pragma unroll
-                for (int ks = 0; ks < 4; ++ks)
+                    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+                        for (int jj = 0; jj < JB; ++jj)
+#pragma unroll
+                            for (int bb = 0; bb < BPW; ++bb) {
+                                const uint4 w4 = wv[jj][bb];
+                                const uint32_t wq = ks == 0 ? w4.x : ks == 1 ? w4.y : ks == 2 ? w4.z : w4.w;
+                                uint32_t a[4];
+                                unscaled_word(wq, a);
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt) {
+                                    if (ks == 0) mma_16816_zero(cc[jj][bb][mt], a, b[jj][mt][0], b[jj][mt][1]);
+                                    else mma_16816(cc[jj][bb][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);
+                                }
+                            }
+                    // C fragment: elements 0, 1 are row g8 of the block, 2, 3 row g8 + 8
 #pragma unroll
                     for (int jj = 0; jj < JB; ++jj)
 #pragma unroll
-                        for (int bb = 0; bb < BPW; ++bb) {
-                            const uint4 w4 = wv[jj][bb];
-                            const uint32_t wq = ks == 0 ? w4.x : ks == 1 ? w4.y : ks == 2 ? w4.z : w4.w;
-                            uint32_t a[4];
-                            dequant_word(wq, s_lo[bb][jb + jj], s_hi[bb][jb + jj], a);
+                        for (int bb = 0; bb < BPW; ++bb)
 #pragma unroll
                             for (int mt = 0; mt < MT; ++mt)
-                                mma_16816(acc[bb][(jb + jj) % CH][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);
-                        }
+#pragma unroll
+                                for (int i = 0; i < 4; ++i) {
+                                    float& d = acc[bb][(jb + jj) % CH][mt][i];
+                                    d = fmaf(i < 2 ? f_lo[bb][jb + jj] : f_hi[bb][jb + jj], cc[jj][bb][mt][i], d);
+                                }
+                } else {
+#pragma unroll
+                    for (int ks = 0; ks < 4; ++ks)
+#pragma unroll
+                        for (int jj = 0; jj < JB; ++jj)
+#pragma unroll
+                            for (int bb = 0; bb < BPW; ++bb) {
+                                const uint4 w4 = wv[jj][bb];
+                                const uint32_t wq = ks == 0 ? w4.x : ks == 1 ? w4.y : ks == 2 ? w4.z : w4.w;
+                                uint32_t a[4];
+                                dequant_word(wq, h_lo[bb][jb + jj], h_hi[bb][jb + jj], a);
+#pragma unroll
+                                for (int mt = 0; mt < MT; ++mt)
+                                    mma_16816(acc[bb][(jb + jj) % CH][mt], a, b[jj][mt][2 * ks], b[jj][mt][2 * ks + 1]);
+                            }
+                }
             }
         }
         // release the stage to the producer
@@ -272,7 +323,7 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
         const int g = st.g;
         const bool whole = st.kc + nk == KC && gkc0 == 0;
         if (st.advance(nk, KC)) {
-            // this CTA's part of group g is done: fold the chains (fixed order) and store
+            // this CTA's part of group g is done: fold the two sets (fixed order) and store
             float* const my = partials + (size_t)part.slot(c, g) * kDcSlotFloats;
 #pragma unroll
             for (int bb = 0; bb < BPW; ++bb) {

@@ -50,6 +50,18 @@ __device__ __forceinline__ void dequant_word(uint32_t q, uint32_t s_lo, uint32_t
     a[3] = hmul2_u32(hsub2_u32(and_or(q8, kHiMask, kHiMagic), kHiBias), s_hi);
 }
 
+// The same word as four half2 registers of the exact integers q - 8 (no scale): the decode
+// path multiplies by the scale after the tensor-core product, in fp32 (see decode.cuh).
+__device__ __forceinline__ void unscaled_word(uint32_t q, uint32_t (&a)[4]) {
+    constexpr uint32_t kLoMask = 0x000F000Fu, kLoMagic = 0x64006400u, kLoBias = 0x64086408u;  // 1024, 1032
+    constexpr uint32_t kHiMask = 0x00F000F0u, kHiMagic = 0x54005400u, kHiBias = 0x54805480u;  // 64, 72
+    const uint32_t q8 = q >> 8;
+    a[0] = hsub2_u32(and_or(q,  kLoMask, kLoMagic), kLoBias);
+    a[1] = hsub2_u32(and_or(q,  kHiMask, kHiMagic), kHiBias);
+    a[2] = hsub2_u32(and_or(q8, kLoMask, kLoMagic), kLoBias);
+    a[3] = hsub2_u32(and_or(q8, kHiMask, kHiMagic), kHiBias);
+}
+
 // Broadcast an fp16 bit pattern into both halves of a half2.
 __device__ __forceinline__ uint32_t bcast_half(uint16_t h) {
     return (uint32_t)h | ((uint32_t)h << 16);
