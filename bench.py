@@ -194,30 +194,16 @@ def barrier(world):
 
 def graph_time_ms(step_fn, steps, warmup, world):
     """Capture one step in a CUDA graph, replay W untimed then K timed; device ms (max over ranks)."""
-    side = torch.cuda.Stream()
-    side.wait_stream(torch.cuda.current_stream())
-    with torch.cuda.stream(side):
-        step_fn()
-    torch.cuda.current_stream().wait_stream(side)
-    torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g):
-        step_fn()
-    for _ in range(warmup):
-        g.replay()
-    torch.cuda.synchronize()
+    from w4a16_opt.timing import GraphStep
+    g = GraphStep(step_fn)
+    g.warm(warmup)
     barrier(world)
     torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
-    for _ in range(steps):
-        g.replay()
-    t1.record()
-    t1.synchronize()
+    ms = g.total_ms(steps)
     torch.cuda.synchronize()
     barrier(world)
-    ms = max_over_ranks(t0.elapsed_time(t1), world)
-    del g
+    ms = max_over_ranks(ms, world)
+    g.close()
     return ms
 
 

@@ -102,29 +102,19 @@ def algorithmic_bytes(M: int, N: int, K: int, G: int) -> int:
 
 
 def graph_time_us(calls, reps: int):
-    """(median, min) microseconds per call: all calls captured in one CUDA graph, which is
-    replayed ``reps`` times between CUDA events on the capturing stream."""
-    for call in calls:
-        call()
-    torch.cuda.synchronize()
-    graph = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(graph):
+    """(median, min) microseconds per call: the calls captured as one CUDA graph
+    (``timing.GraphStep``), each of ``reps`` replays timed on its own."""
+    from .timing import GraphStep
+
+    def step():
         for call in calls:
             call()
-    for _ in range(3):
-        graph.replay()
-    torch.cuda.synchronize()
-    samples = []
-    for _ in range(reps):
-        t0 = torch.cuda.Event(enable_timing=True)
-        t1 = torch.cuda.Event(enable_timing=True)
-        t0.record()
-        graph.replay()
-        t1.record()
-        t1.synchronize()
-        samples.append(t0.elapsed_time(t1) * 1e3 / len(calls))
-    del graph
-    return statistics.median(samples), min(samples)
+
+    g = GraphStep(step)
+    g.warm(3)
+    per_call = [ms * 1e3 / len(calls) for ms in g.each_ms(reps)]
+    g.close()
+    return statistics.median(per_call), min(per_call)
 
 
 def make_weights(N: int, K: int, G: int, target_mib: float, device, seed: int = 0):
