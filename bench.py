@@ -262,10 +262,11 @@ def run_ours(args):
                                       for u in units))
     torch.cuda.synchronize()
 
-    def make_step(resident):
+    def make_step(resident, fp32_scale=False):
         def step():
             for u in units:
-                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws, weights_resident=resident)
+                w4a16_opt.w4a16_gemm_out(u["Wp"], u["x"], u["s"], u["y"], workspace=ws, weights_resident=resident,
+                                         fp32_scale=fp32_scale)
         return step
 
     # kernels of ours per step: one decode_kernel per GEMM (+ its combine kernel when a column
@@ -284,6 +285,12 @@ def run_ours(args):
                     "ms_per_step": round(ms_default / args.steps, 5),
                     "mode": "plain stream order: each GEMM reads its weights only after the previous kernel "
                             "on the stream has completed (w4a16_gemm default)"}
+    ms_fs = graph_time_ms(make_step(True, True), args.steps, args.warmup, world)
+    fp32_scale_mode = {"value": round(world * step_bytes * args.steps / (ms_fs / 1e3) / 1e9, 2), "unit": "GB/s",
+                       "ms_per_step": round(ms_fs / args.steps, 5),
+                       "mode": "weights resident + W4A16_FLAG_FP32_SCALE: for M <= 8 the group scales are applied "
+                               "in fp32 after the tensor-core products (not the reference's bit-identical fp16 "
+                               "dequantised weights; opt-in)"}
 
     # ---- e2e through the public API: every step copies its activations in from pinned host
     # memory (one transfer), makes the 16 calls into one output buffer and reads it back (one
@@ -442,7 +449,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": round(ms_step, 5), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f16",
         "data": "synthetic (seeded: x~N(0,1) fp16, q~U{0..15}, scales~U[0.002,0.02] fp16)",
-        "config": config, "default_mode": default_mode,
+        "config": config, "default_mode": default_mode, "fp32_scale_mode": fp32_scale_mode,
         "e2e": e2e, "host_us_per_call": host_us, "roofline": roofline, "prefill": prefill, "cpu_baseline": cpu,
         "gpu_reference": gpu_ref, "tp70b": tp70b, "clocks": clocks.summary(),
         "gpu_launches": launches_per_step * args.steps,

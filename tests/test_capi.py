@@ -92,6 +92,13 @@ def test_gemm_null_pointers_rejected():
     assert st == 1 and "non-null" in capi.last_error(lib)
 
 
+def test_gemm_unknown_flags_rejected():
+    lib = capi.load()
+    p = ctypes.c_void_p(0x10000)
+    st = lib.w4a16_gemm_ex(p, p, p, p, 2, 64, 512, 8, 64 * 512 // 8, -1, 0, 4, None, 0, None)
+    assert st == 17 and "unknown flag bits 4" in capi.last_error(lib)
+
+
 def test_gemm_bad_out_dtype_rejected():
     lib = capi.load()
     p = ctypes.c_void_p(0x10000)
@@ -136,6 +143,8 @@ def test_header_layout_matches_ctypes(tmp_path):
              '    printf("sizeof %zu\\n", sizeof(w4a16_route));']
     lines += [f'    printf("{f} %zu\\n", offsetof(w4a16_route, {f}));' for f in fields]
     lines += [f'    printf("{name} %d\\n", (int){name});' for name in capi.STATUS_NAMES.values()]
+    lines += ['    printf("W4A16_FLAG_WEIGHTS_RESIDENT %d\\n", (int)W4A16_FLAG_WEIGHTS_RESIDENT);',
+              '    printf("W4A16_FLAG_FP32_SCALE %d\\n", (int)W4A16_FLAG_FP32_SCALE);']
     lines += ['    printf("W4A16_OUT_F32 %d\\n", (int)W4A16_OUT_F32);',
               '    printf("W4A16_ABI_VERSION %d\\n", (int)W4A16_ABI_VERSION);', "    return 0;", "}"]
     src.write_text("\n".join(lines) + "\n")
@@ -150,6 +159,8 @@ def test_header_layout_matches_ctypes(tmp_path):
     for code, name in capi.STATUS_NAMES.items():
         assert int(out[name]) == code, name
     assert int(out["W4A16_OUT_F32"]) == capi.W4A16_OUT_F32
+    assert int(out["W4A16_FLAG_WEIGHTS_RESIDENT"]) == capi.W4A16_FLAG_WEIGHTS_RESIDENT
+    assert int(out["W4A16_FLAG_FP32_SCALE"]) == capi.W4A16_FLAG_FP32_SCALE
     assert int(out["W4A16_ABI_VERSION"]) == capi.load().w4a16_abi_version()
 
 

@@ -434,6 +434,45 @@ def test_weights_resident_flag_same_result():
         assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("G", GS)
+@pytest.mark.parametrize("M", [1, 3, 8, 9, 16])
+@pytest.mark.parametrize("N,K", [(4096, 4096), (1024, 4096), (272, 1152)])
+def test_fp32_scale_flag(M, N, K, G):
+    """W4A16_FLAG_FP32_SCALE: within the tolerance of the reference GEMM, at least as close
+    to the exact float64 product as the default (its weights are not rounded to fp16), and
+    a no-op for M > 8."""
+    from w4a16_opt import w4a16_gemm_out
+    x, q, s, Wp = make_problem(M, N, K, G, seed=M * 7 + N)
+    ref = ref_gemm(x, q, s, G)
+    a = w4a16_gemm_out(Wp, x, s, torch.empty(M, N, dtype=torch.half, device="cuda"))
+    b = w4a16_gemm_out(Wp, x, s, torch.empty(M, N, dtype=torch.half, device="cuda"), fp32_scale=True)
+    assert_close(b, ref)
+    if M > 8:
+        assert torch.equal(a, b)
+        return
+    w64 = (to_np(q).astype(np.float64) - 8.0) * np.repeat(to_np(s).astype(np.float64).T, G, axis=1)
+    exact = to_np(x).astype(np.float64) @ w64.T
+    err = lambda y: np.linalg.norm(to_np(y).astype(np.float64) - exact)
+    assert err(b) <= err(a) * 1.05 + 1e-6
+
+
+@pytest.mark.parametrize("G", GS)
+def test_fp32_scale_onehot_exact(G):
+    """x = e_k gives column k of the dequantised weights exactly with the flag too: the fp32
+    product (q - 8) * s is exact and rounds once to the reference's fp16 value."""
+    from w4a16_opt import w4a16_gemm_out
+    N, K = 256, 1024
+    _, q, s, Wp = make_problem(1, N, K, G)
+    Wd = torch.from_numpy(oracle.dequantize_w4(to_np(q), to_np(s), G)).cuda()
+    for k in (0, 1, 63, 64, 127, 513, 1023):
+        for m in (1, 8):
+            x = torch.zeros(m, K, dtype=torch.half, device="cuda")
+            x[m - 1, k] = 1
+            y = w4a16_gemm_out(Wp, x, s, torch.empty(m, N, dtype=torch.half, device="cuda"), fp32_scale=True)
+            assert torch.equal(y[m - 1], Wd[:, k])
+            assert not y[:m - 1].any()
+
+
 def test_device_status_clean():
     """No kernel in this session hit a bounded-wait timeout."""
     from w4a16_opt import device_status

@@ -138,14 +138,14 @@ w4a16_status w4a16_gemm_ex(const int32_t* Wp, const void* x, const void* scales,
     if (!Wp || !x || !scales || !y) return fail(W4A16_ERR_NULL_POINTER, "Wp, x, scales and y must be non-null");
     if (out_dtype != W4A16_OUT_F16 && out_dtype != W4A16_OUT_F32)
         return fail(W4A16_ERR_OUT_DTYPE, "out_dtype must be 0 (fp16) or 1 (fp32)");
-    if (flags & ~(uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT)
-        return fail(W4A16_ERR_FLAGS, "unknown flag bits " + std::to_string(flags & ~(uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT));
+    constexpr uint32_t kKnownFlags = W4A16_FLAG_WEIGHTS_RESIDENT | W4A16_FLAG_FP32_SCALE;
+    if (flags & ~kKnownFlags) return fail(W4A16_ERR_FLAGS, "unknown flag bits " + std::to_string(flags & ~kKnownFlags));
     w4a16::DeviceInfo d;
     if ((s = check_device(&d)) != W4A16_OK) return s;
     const int G = (int)(K / groups);
     w4a16::GemmArgs a{Wp, x, scales, y, (int)M, (int)N, (int)K, G, out_dtype == W4A16_OUT_F32,
                       static_cast<cudaStream_t>(stream), pdl_enabled(), (flags & W4A16_FLAG_WEIGHTS_RESIDENT) != 0,
-                      workspace, (size_t)workspace_bytes};
+                      (flags & W4A16_FLAG_FP32_SCALE) != 0, workspace, (size_t)workspace_bytes};
     const Route r = make_route(a.M, a.N, a.K, G, variant, d);
     const size_t need = route_workspace(r);
     if (need > 0) {

@@ -18,12 +18,12 @@
 //     far better than 512-byte pieces -- the token rows of the step's chunks in
 //     one box (128-byte swizzle, rows >= M zero-filled) and the group's scales.
 //   * Consumer warp w owns n16 blocks 2w and 2w+1 of the group.  The packed word
-//     of each lane is already an m16n8k16 A fragment, fed to mma.sync directly
+//     of each lane is already an m16n8k16 A fragment, so the exact 13-instruction
+//     dequant (the reference's fp16 values, bit for bit) feeds mma.sync directly
 //     (weights = A, the <= 16 tokens = the n8 side; one activation fragment serves
-//     both blocks).  For M <= 8 the fragment holds the exact integers q - 8 (9
-//     instructions: 1 shift, 4 LOP3, 4 HSUB2) and each chunk's products are scaled in
-//     fp32 after the tensor core, one FMA per accumulator element; for M > 8 it holds
-//     the exact fp16 (q - 8) * s (13 instructions).
+//     both blocks).  With W4A16_FLAG_FP32_SCALE and M <= 8 the fragment holds the
+//     exact integers q - 8 instead (9 instructions) and each chunk's products are
+//     scaled in fp32 after the tensor core, one FMA per accumulator element.
 //   * A CTA's columns are complete in registers when it leaves a group: a group
 //     covered by one CTA is written to y directly; a group split across CTAs
 //     leaves one fp32 partial per CTA in the caller's workspace, and
@@ -91,7 +91,7 @@ inline DcPartition dc_partition(int N, int K, int num_sms) {
     return cache[key] = dc_cut(N, K, num_sms);
 }
 
-template <int G, int MP, bool OUT_F32>
+template <int G, int MP, bool OUT_F32, bool FP32_SCALE>
 __global__ void __launch_bounds__(kDcThreads, 1)
 decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CUtensorMap tx,
               const __grid_constant__ CUtensorMap ts, void* __restrict__ yv, int M, int N, int box_blocks,
@@ -189,17 +189,18 @@ decode_kernel(const __grid_constant__ CUtensorMap tw, const __grid_constant__ CU
     }
 
     // ---------------------------------------------------- consumer warp: n16 blocks 2*warp, 2*warp+1 of each group
-    // M <= 8 (MT = 1): per 64-wide chunk and n16 block, a chain of four m16n8k16 products of
-    // the exact integers q - 8 (fp16) with the activations, started from zero, then one fp32
-    // FMA per accumulator element by the chunk's scale (a chunk never straddles two scale
-    // groups: G is a multiple of 64).  9 instructions dequantise a word.
-    // M > 8 (MT = 2): each word is dequantised exactly to fp16 (q - 8) * s, 13 instructions,
-    // and the products accumulate directly.  With twice the tensor-core work per word, the
-    // per-chunk scaling measured slower here (q/o 9.6 against 7.8 us at M = 16).
+    // Default: each word is dequantised exactly to the reference's fp16 (q - 8) * s (13
+    // instructions) and the products accumulate directly.
+    // FP32_SCALE, M <= 8 (MT = 1): per 64-wide chunk and n16 block, a chain of four m16n8k16
+    // products of the exact integers q - 8 (fp16; 9 instructions a word) with the
+    // activations, started from zero, then one fp32 FMA per accumulator element by the
+    // chunk's scale (a chunk never straddles two scale groups: G is a multiple of 64).  Not
+    // used for M > 8: with twice the tensor-core work per word it measured slower there (q/o
+    // 9.6 against 7.8 us at M = 16).
     // Either way a block's sums alternate between two accumulator sets, added at the end.
     constexpr int BPW = kDcBPW;
     constexpr int CH = 2;
-    constexpr bool SCALE_AFTER = MT == 1;
+    constexpr bool SCALE_AFTER = FP32_SCALE && MT == 1;
     const int g8 = lane >> 2, t4 = lane & 3;
     pdl_wait();   // the workspace and y may still be in use by the previous kernel
 
@@ -418,10 +419,10 @@ size_t decode_workspace_bytes(int N, int K, const DeviceInfo& dev) {
 cudaError_t make_decode_tensor_maps(const GemmArgs& a, int box_blocks, int box_chunks, int mp, CUtensorMap* tw,
                                     CUtensorMap* tx, CUtensorMap* ts);
 
-template <int G, int MP, bool F32>
+template <int G, int MP, bool F32, bool FS>
 static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     (void)p;
-    auto kern = decode_kernel<G, MP, F32>;
+    auto kern = decode_kernel<G, MP, F32, FS>;
     cudaError_t err = ensure_max_dynamic_smem(reinterpret_cast<const void*>(kern));
     if (err != cudaSuccess) return err;
     DeviceInfo dev;
@@ -458,14 +459,21 @@ static cudaError_t launch_decode_t(const GemmArgs& a, const DecodePlan& p) {
     return cudaLaunchKernelEx(&fc, decode_combine_kernel<F32>, a.y, a.N, part, static_cast<const float*>(partials));
 }
 
+template <int G, int MP, bool F32>
+static cudaError_t launch_decode_fs(const GemmArgs& a, const DecodePlan& p) {
+    // the fp32-scale form exists for M <= 8 only (MP = 8)
+    if (MP == 8 && a.fp32_scale) return launch_decode_t<G, MP, F32, MP == 8>(a, p);
+    return launch_decode_t<G, MP, F32, false>(a, p);
+}
+
 cudaError_t launch_decode(const GemmArgs& a, const DecodePlan& p) {
     const bool f32 = a.out_f32;
     if (a.G == 64) {
-        if (p.mt == 1) return f32 ? launch_decode_t<64, 8, true>(a, p) : launch_decode_t<64, 8, false>(a, p);
-        return f32 ? launch_decode_t<64, 16, true>(a, p) : launch_decode_t<64, 16, false>(a, p);
+        if (p.mt == 1) return f32 ? launch_decode_fs<64, 8, true>(a, p) : launch_decode_fs<64, 8, false>(a, p);
+        return f32 ? launch_decode_fs<64, 16, true>(a, p) : launch_decode_fs<64, 16, false>(a, p);
     }
-    if (p.mt == 1) return f32 ? launch_decode_t<128, 8, true>(a, p) : launch_decode_t<128, 8, false>(a, p);
-    return f32 ? launch_decode_t<128, 16, true>(a, p) : launch_decode_t<128, 16, false>(a, p);
+    if (p.mt == 1) return f32 ? launch_decode_fs<128, 8, true>(a, p) : launch_decode_fs<128, 8, false>(a, p);
+    return f32 ? launch_decode_fs<128, 16, true>(a, p) : launch_decode_fs<128, 16, false>(a, p);
 }
 
 }  // namespace w4a16

@@ -20,6 +20,7 @@ struct GemmArgs {
     bool pdl;             // launch with programmatic dependent launch enabled
     bool weights_resident;// wp/scales are not written by the kernel launched just before:
                           // the decode producer may fetch them before griddepcontrol.wait
+    bool fp32_scale;      // decode, M <= 8: scales applied in fp32 after the MMA (W4A16_FLAG_FP32_SCALE)
     void* workspace;      // decode scratch (split-group partials); no initial contents needed
     size_t workspace_bytes;
 };

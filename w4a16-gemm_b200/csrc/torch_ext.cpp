@@ -109,9 +109,10 @@ torch::Tensor w4a16_gemm_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor sca
 // `workspace` (optional): a CUDA buffer of >= workspace_bytes(...) bytes (scratch) that the
 // caller keeps for calls issued in stream order; otherwise the binding supplies one.
 // `weights_resident`: Wp and scales are not written by the kernel launched just before
-// (W4A16_FLAG_WEIGHTS_RESIDENT).
+// (W4A16_FLAG_WEIGHTS_RESIDENT).  `fp32_scale`: W4A16_FLAG_FP32_SCALE.
 torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor scales, torch::Tensor y,
-                                int64_t variant, c10::optional<torch::Tensor> workspace, bool weights_resident) {
+                                int64_t variant, c10::optional<torch::Tensor> workspace, bool weights_resident,
+                                bool fp32_scale) {
     check_tensors(Wp, x, scales);
     TORCH_CHECK(y.is_cuda() && y.device() == x.device(), "y must be a CUDA tensor on x's device");
     TORCH_CHECK(y.is_contiguous(), "contiguous only");
@@ -120,7 +121,8 @@ torch::Tensor w4a16_gemm_out_py(torch::Tensor Wp, torch::Tensor x, torch::Tensor
     const int32_t v = clamp_variant(variant);
     check(w4a16_validate(Wp.data_ptr(), x.data_ptr(), scales.data_ptr(), x.size(0), scales.size(1), x.size(1),
                          scales.size(0), Wp.numel(), v));
-    run(Wp, x, scales, y, v, workspace, weights_resident ? (uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT : 0u);
+    run(Wp, x, scales, y, v, workspace,
+        (weights_resident ? (uint32_t)W4A16_FLAG_WEIGHTS_RESIDENT : 0u) | (fp32_scale ? (uint32_t)W4A16_FLAG_FP32_SCALE : 0u));
     return y;
 }
 
@@ -206,7 +208,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
     m.def("w4a16_gemm_out", &w4a16_gemm_out_py, "W4A16 GEMM into a preallocated fp16/fp32 output",
           pybind11::arg("Wp"), pybind11::arg("x"), pybind11::arg("scales"), pybind11::arg("y"),
           pybind11::arg("variant") = -1, pybind11::arg("workspace") = pybind11::none(),
-          pybind11::arg("weights_resident") = false);
+          pybind11::arg("weights_resident") = false, pybind11::arg("fp32_scale") = false);
     m.def("workspace_bytes", &workspace_bytes_py, "workspace bytes a GEMM call needs on the current device",
           pybind11::arg("M"), pybind11::arg("N"), pybind11::arg("K"), pybind11::arg("groups"),
           pybind11::arg("variant") = -1);

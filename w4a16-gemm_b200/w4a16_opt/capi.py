@@ -16,6 +16,7 @@ W4A16_OK = 0
 W4A16_OUT_F16 = 0
 W4A16_OUT_F32 = 1
 W4A16_FLAG_WEIGHTS_RESIDENT = 1
+W4A16_FLAG_FP32_SCALE = 2
 
 STATUS_NAMES = {
     0: "W4A16_OK", 1: "W4A16_ERR_NULL_POINTER", 2: "W4A16_ERR_VARIANT", 3: "W4A16_ERR_M",

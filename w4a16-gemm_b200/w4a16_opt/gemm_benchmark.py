@@ -58,6 +58,8 @@ def parse_args(argv=None) -> argparse.Namespace:
     ap.add_argument("--reps", type=int, default=30)
     ap.add_argument("--json", default=None, help="result JSON path (default: print the document)")
     ap.add_argument("--md", action="store_true", help="print a Markdown table")
+    ap.add_argument("--fp32-scale", action="store_true",
+                    help="decode path, M <= 8: apply scales in fp32 after the products (W4A16_FLAG_FP32_SCALE)")
     return ap.parse_args(argv)
 
 
@@ -148,18 +150,22 @@ def route_name(M: int, N: int, K: int, G: int) -> str:
 
 
 def run(shapes, phase_m: dict, G: int, target_mib: float, reps: int, device="cuda", timer=graph_time_us,
-        route=route_name, log=print) -> list:
+        route=route_name, log=print, fp32_scale: bool = False) -> list:
     """Rows for every (layer, mode, M), in the reference's loop order (layer outermost).
     ``timer(calls, reps) -> (median_us, min_us)`` and ``route(M, N, K, G) -> str`` are the
-    device-side steps."""
-    from . import w4a16_gemm
+    device-side steps.  ``fp32_scale`` selects W4A16_FLAG_FP32_SCALE for every call."""
+    from . import w4a16_gemm, w4a16_gemm_out
     rows = []
     for layer, (N, K) in shapes:
         weights = make_weights(N, K, G, target_mib, device)
         for mode, ms in phase_m.items():
             for M in ms:
                 x = torch.randn((M, K), device=device, dtype=torch.float16)
-                calls = [lambda w=w, s=s: w4a16_gemm(w, x, s, variant=-1) for w, s in weights]
+                if fp32_scale:
+                    y = torch.empty((M, N), device=device, dtype=torch.float16)
+                    calls = [lambda w=w, s=s: w4a16_gemm_out(w, x, s, y, fp32_scale=True) for w, s in weights]
+                else:
+                    calls = [lambda w=w, s=s: w4a16_gemm(w, x, s, variant=-1) for w, s in weights]
                 median_us, min_us = timer(calls, reps)
                 rows.append(make_row(mode, layer, N, K, M, G, median_us, min_us, route(M, N, K, G)))
                 log(f"finished {mode} {layer} M={M}")
@@ -225,7 +231,7 @@ def main(argv=None) -> dict:
     device = device_facts()
     print(f"# {device['name']}  SMs={device['sms']}  torch={torch.__version__} cuda={torch.version.cuda}  "
           f"weight working set={args.target_mb:.0f} MiB")
-    rows = run(shapes, phase_m, args.G, args.target_mb, args.reps)
+    rows = run(shapes, phase_m, args.G, args.target_mb, args.reps, fp32_scale=args.fp32_scale)
     doc = document(shapes, phase_m, args.G, args.target_mb, args.reps, rows, device)
     if args.json:
         os.makedirs(os.path.dirname(os.path.abspath(args.json)), exist_ok=True)
