@@ -2,17 +2,19 @@
 
 The counterpart, for this package's tcgen05 prefill kernel, of the reference's numpy
 emulation of its own prefill kernel (akshay919191/W4A16-GEMM tests/layout_prefill.py).
-One CTA walks every (token tile, 128-row tile) and every 64-wide k-step as prefill_kernel
-does (csrc/prefill.cuh):
+One CTA walks every (token tile, 128-row tile) and every pipeline stage as prefill_kernel
+does (csrc/prefill.cuh); a stage holds KCH 64-wide K chunks (KCH = pf_kch(TOK): 4, 4, 3, 2
+for 32, 64, 128, 256-token tiles; a last stage may hold fewer):
 
-* Dequant warps 2..9 each take n16 block `nbl = 2 (warp & 3) + (qi & 1)` of the step's
-  packed words and scales. They dequantise with the kernel's bit tricks and store the 16
-  registers with `tcgen05.st.16x128b.x8` into the A ring: TMEM lane base 16 nbl, columns
-  A_COL0 + slot * 32.
-* The MMA of each 16-wide k slice reads A from TMEM columns + 8 k16. It reads B as the
-  step's activation rows, through a K-major 128-byte-swizzle descriptor advanced by 32 bytes
-  per slice. It accumulates into columns b * TOK of the fp32 accumulator, overwriting on
-  the first slice of a tile.
+* Dequant warps 2..9 each take n16 block `nbl = 2 (warp & 3) + (qi & 1)` of every chunk's
+  packed words and scales ([block][chunk][512 B] and [chunk][128] in the stage). They
+  dequantise with the kernel's bit tricks and store each chunk's 16 registers with
+  `tcgen05.st.16x128b.x8` into the A ring: TMEM lane base 16 nbl, columns
+  A_COL0 + slot * 32 KCH + 32 chunk.
+* The MMA of each chunk's 16-wide k slices reads A from the chunk's TMEM columns + 8 k16.
+  It reads B as the chunk's activation rows, through a K-major 128-byte-swizzle descriptor
+  advanced by 32 bytes per slice. It accumulates into columns b * TOK of the fp32
+  accumulator, overwriting on the first slice of a tile, in K order.
 * Epilogue warp (quarter q = warp & 3, part h) reads TMEM lanes 32q..32q+31 and token
   columns h * TOK/4 .. (h + 1) * TOK/4 - 1 and stores row n = 128 tn + 32q + lane,
   tokens TOK tt + h * TOK/4 + j, guarded by N and M.
@@ -36,10 +38,15 @@ from oracle import w4a16_oracle as oracle
 ROWS, DQ_WARP0, DQ_WARPS, EPI_WARP0, EPI_WARPS = 128, 2, 8, 10, 16
 
 
+def pf_kch(TOK):
+    return 4 if TOK <= 64 else 3 if TOK == 128 else 2
+
+
 def cfg(TOK):
     accs = 2 if TOK <= 128 else 1
     a_col0 = accs * TOK
-    return accs, a_col0, min((512 - a_col0) // 32, 8)
+    a_cols = 32 * pf_kch(TOK)
+    return accs, a_col0, min((512 - a_col0) // a_cols, 8), pf_kch(TOK), a_cols
 
 
 def dequant16(words, s_lo, s_hi):
@@ -65,7 +72,8 @@ def emulate(Wp, x, scales, N, K, G, TOK):
     M = x.shape[0]
     NB, KC = N // 16, K // 64
     Wp4 = Wp.view(np.uint32).reshape(NB, KC, 32, 4)
-    accs, a_col0, na = cfg(TOK)
+    accs, a_col0, na, kch, a_cols = cfg(TOK)
+    KT = (KC + kch - 1) // kch
     n_tiles, t_tiles = (N + ROWS - 1) // ROWS, (M + TOK - 1) // TOK
     tmem = np.full((ROWS, 512, 2), np.nan)                  # [lane][column][half]
     y = np.full((M, N), np.nan)
@@ -74,43 +82,55 @@ def emulate(Wp, x, scales, N, K, G, TOK):
     for tc, tile in enumerate(range(n_tiles * t_tiles)):
         tt, tn = tile // n_tiles, tile % n_tiles
         b = tc % accs
-        for kt in range(KC):
+        for kt in range(KT):
             a = it % na
             it += 1
-            # the stage: packed words of blocks 8 tn .. 8 tn + 7 (zero past N), scale row, x rows
-            words = np.zeros((8, 32, 4), np.uint32)
+            nch = min(kch, KC - kt * kch)
+            KB = min(kch, KC)
+            # the stage's weight box {128 words, KB chunks, 8 blocks} as the tensor copy lays it
+            # out: [block][chunk][32 lanes x 4 words], zeros past K and past N
+            wimg = np.zeros(8 * KB * 128, np.uint32)
             for nbl in range(8):
-                if tn * 8 + nbl < NB:
-                    words[nbl] = Wp4[tn * 8 + nbl, kt]
-            srow = np.zeros(ROWS, np.float16)
-            cols = np.arange(tn * ROWS, tn * ROWS + ROWS)
-            srow[cols < N] = scales[(kt * 64) // G, cols[cols < N]]
-            xt = np.zeros((TOK, 64), np.float64)
-            rows = np.arange(tt * TOK, tt * TOK + TOK)
-            xt[rows < M] = x[rows[rows < M], kt * 64:(kt + 1) * 64]
-            # dequant warps -> TMEM A slot
-            fresh = np.zeros((ROWS, 32), bool)
-            for warp in range(DQ_WARP0, DQ_WARP0 + DQ_WARPS):
-                qi = (warp - 2) >> 2
-                nbl = 2 * (warp & 3) + (qi & 1)
-                for L in range(32):
-                    g = L >> 2
-                    regs = dequant16(words[nbl, L], srow[nbl * 16 + g], srow[nbl * 16 + g + 8])
-                    for R, (lo, hi) in enumerate(regs):
-                        lane = 16 * nbl + L // 4 + 8 * (R % 2)
-                        col = a_col0 + a * 32 + 4 * (R // 2) + (L % 4)
-                        check_lane(warp, lane)
-                        assert a_col0 <= col < 512, "A store outside the A ring"
-                        tmem[lane, col] = (lo, hi)
-                        fresh[lane, col - a_col0 - a * 32] = True
-            assert fresh.all(), "an A column the MMA reads was not written this k-step"
-            # MMA: 4 slices of 16 k
-            for k16 in range(4):
-                cols_a = a_col0 + a * 32 + k16 * 8 + np.arange(8)
-                A = tmem[:, cols_a, :].reshape(ROWS, 16)            # lane i = row i, 2 k per column
-                B = xt[:, k16 * 16:(k16 + 1) * 16].T                # [16 k, TOK]
-                D = tmem[:, b * TOK:(b + 1) * TOK, 0]
-                tmem[:, b * TOK:(b + 1) * TOK, 0] = A @ B + (D if (kt | k16) != 0 else 0.0)
+                for jj in range(KB):
+                    if tn * 8 + nbl < NB and kt * kch + jj < KC:
+                        wimg[(nbl * KB + jj) * 128:(nbl * KB + jj + 1) * 128] = Wp4[tn * 8 + nbl, kt * kch + jj].reshape(-1)
+            fresh = np.zeros((ROWS, a_cols), bool)
+            xts = []
+            for j in range(nch):
+                kc = kt * kch + j
+                # chunk j of the stage: its scale row and x rows; the packed words are read from
+                # the stage image at the dequant warps' address (nbl * KB + j) * 512 + lane * 16
+                srow = np.zeros(ROWS, np.float16)
+                cols = np.arange(tn * ROWS, tn * ROWS + ROWS)
+                srow[cols < N] = scales[(kc * 64) // G, cols[cols < N]]
+                xt = np.zeros((TOK, 64), np.float64)
+                rows = np.arange(tt * TOK, tt * TOK + TOK)
+                xt[rows < M] = x[rows[rows < M], kc * 64:(kc + 1) * 64]
+                xts.append(xt)
+                # dequant warps -> TMEM A slot, chunk j's 32 columns
+                for warp in range(DQ_WARP0, DQ_WARP0 + DQ_WARPS):
+                    qi = (warp - 2) >> 2
+                    nbl = 2 * (warp & 3) + (qi & 1)
+                    for L in range(32):
+                        g = L >> 2
+                        off = ((nbl * KB + j) * 512 + L * 16) // 4
+                        regs = dequant16(wimg[off:off + 4], srow[nbl * 16 + g], srow[nbl * 16 + g + 8])
+                        for R, (lo, hi) in enumerate(regs):
+                            lane = 16 * nbl + L // 4 + 8 * (R % 2)
+                            col = a_col0 + a * a_cols + j * 32 + 4 * (R // 2) + (L % 4)
+                            check_lane(warp, lane)
+                            assert a_col0 <= col < 512, "A store outside the A ring"
+                            tmem[lane, col] = (lo, hi)
+                            fresh[lane, col - a_col0 - a * a_cols] = True
+            assert fresh[:, :32 * nch].all(), "an A column the MMA reads was not written this stage"
+            # MMA: per chunk, 4 slices of 16 k, in K order
+            for j in range(nch):
+                for k16 in range(4):
+                    cols_a = a_col0 + a * a_cols + j * 32 + k16 * 8 + np.arange(8)
+                    A = tmem[:, cols_a, :].reshape(ROWS, 16)        # lane i = row i, 2 k per column
+                    B = xts[j][:, k16 * 16:(k16 + 1) * 16].T        # [16 k, TOK]
+                    D = tmem[:, b * TOK:(b + 1) * TOK, 0]
+                    tmem[:, b * TOK:(b + 1) * TOK, 0] = A @ B + (D if (kt | j | k16) != 0 else 0.0)
         # epilogue warps
         cw = TOK // (EPI_WARPS // 4)
         for warp in range(EPI_WARP0, EPI_WARP0 + EPI_WARPS):
@@ -129,11 +149,13 @@ def emulate(Wp, x, scales, N, K, G, TOK):
 
 
 CASES = [
-    # M, N, K, G, TOK: ragged M and N, every token tile, both group sizes
+    # M, N, K, G, TOK: ragged M and N, every token tile, both group sizes; stages of
+    # 4 + 2, 4, 3 + 1 and 2 + 1 chunks (a last partial stage), one chunk only
     (17, 208, 384, 64, 32),
     (100, 272, 256, 128, 64),
-    (129, 128, 192, 64, 128),
-    (40, 384, 128, 128, 256),
+    (129, 128, 256, 64, 128),
+    (40, 384, 320, 64, 256),
+    (20, 144, 64, 64, 128),
 ]
 
 
@@ -164,7 +186,11 @@ def test_emulation_constants_match_kernel_sources():
     assert (2, 8 * phases, 2 + 8 * phases, epi) == (DQ_WARP0, DQ_WARPS, EPI_WARP0, EPI_WARPS)
     assert int(re.search(r"constexpr int kPfRows = (\d+);", src).group(1)) == ROWS
     assert "ACCS = TOK <= 128 ? 2 : 1" in src and "A_COL0 = ACCS * TOK" in src
-    assert "(512 - A_COL0) / 32 < 8 ? (512 - A_COL0) / 32 : 8" in src
+    assert "A_COLS = 32 * KCH" in src and "(512 - A_COL0) / A_COLS < 8 ? (512 - A_COL0) / A_COLS : 8" in src
+    assert "return tok <= 64 ? W4A16_PF_KCH_SMALL : tok == 128 ? W4A16_PF_KCH_128 : 2;" in src
+    assert [define("W4A16_PF_KCH_SMALL"), define("W4A16_PF_KCH_128")] == [pf_kch(32), pf_kch(128)]
     assert "const int nbl = 2 * (warp & 3) + (qi & 1);" in src
-    assert "tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * 32), r);" in src
-    assert "tc_mma_ts(d, at + k16 * 8, pf_sw128_desc(xa + k16 * 32), idesc, (kt | k16) != 0);" in src
+    assert "tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * C::A_COLS + j * 32), r[j]);" in src
+    assert "w[j] = lds128(sbw + (uint32_t)((nbl * KB + j) * 512 + lane * 16));" in src
+    assert ("tc_mma_ts(d, at + j * 32 + k16 * 8, pf_sw128_desc(xa + j * C::X_CHUNK + k16 * 32), idesc,\n"
+            "                                      (kt | j | k16) != 0);") in src

@@ -154,12 +154,13 @@ cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx
         k.box[0] = 64; k.box[1] = (uint32_t)tok;
         if ((err = encode_tiled(k, tx)) != cudaSuccess) return err;
     }
-    {   // packed words viewed as [NB][KC][128] int32, box {128, 1, 8}
+    {   // packed words viewed as [NB][KC][128] int32, box {128, min(pf_kch(tok), KC), 8}: a stage's
+        // chunks of 8 n16 blocks, each block's chunks one contiguous run
         TmapKey k = tmap_key(a.wp, 3, CU_TENSOR_MAP_DATA_TYPE_INT32, CU_TENSOR_MAP_SWIZZLE_NONE,
                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B);
         k.dims[0] = 128; k.dims[1] = (uint64_t)(a.K / 64); k.dims[2] = (uint64_t)(a.N / 16);
         k.strides[0] = 512; k.strides[1] = (uint64_t)(a.K / 64) * 512;
-        k.box[0] = 128; k.box[1] = 1; k.box[2] = 8;
+        k.box[0] = 128; k.box[1] = (uint32_t)std::min(pf_kch(tok), a.K / 64); k.box[2] = 8;
         if ((err = encode_tiled(k, tw)) != cudaSuccess) return err;
     }
     {   // scales [K/G, N] fp16, box {128, 1}

@@ -60,16 +60,35 @@ constexpr int kPfThreads = (kPfEpiWarp0 + kPfEpiWarps) * 32;
 constexpr int kPfRows = 128;                 // output channels per tile (UMMA M)
 constexpr int kPfWBytes = 8 * 512;           // packed words: 8 n16 blocks x one 64-k chunk
 constexpr int kPfSBytes = kPfRows * 2;       // one fp16 scale row slice
+// 64-wide K chunks per pipeline stage.  A stage's round trip through the rings (tensor copy
+// -> dequant -> TMEM store -> MMA -> commit -> slot free) has a fixed latency, so at small M,
+// where that chain and not the tensor core sets the pace, more chunks per stage means
+// fewer trips per K.  The chunks are still multiplied in K order, one k16 step at a time.
+// Per token tile: as many as keep at least 3 stages in shared memory and 2 A slots in TMEM.
+#ifndef W4A16_PF_KCH_SMALL
+#define W4A16_PF_KCH_SMALL 4
+#endif
+#ifndef W4A16_PF_KCH_128
+#define W4A16_PF_KCH_128 3
+#endif
+__host__ __device__ constexpr int pf_kch(int tok) {
+    return tok <= 64 ? W4A16_PF_KCH_SMALL : tok == 128 ? W4A16_PF_KCH_128 : 2;
+}
 constexpr int kPfSmemBudget = 227 * 1024;    // opt-in dynamic shared memory per CTA on sm_100
 
 template <int TOK>
 struct PfCfg {
     static_assert(TOK == 32 || TOK == 64 || TOK == 128 || TOK == 256, "token tile");
-    static constexpr int X_BYTES = TOK * 128;                         // TOK rows x 64 fp16
-    static constexpr int STAGE = (X_BYTES + kPfWBytes + kPfSBytes + 1023) / 1024 * 1024;
+    static constexpr int KCH = pf_kch(TOK);                           // 64-wide K chunks per stage
+    static constexpr int X_CHUNK = TOK * 128;                         // TOK rows x 64 fp16 (one chunk)
+    static constexpr int X_BYTES = KCH * X_CHUNK;                     // [chunk][TOK rows][128 B]
+    static constexpr int W_BYTES = KCH * kPfWBytes;                   // [n16 block][chunk][512 B]
+    static constexpr int S_BYTES = KCH * kPfSBytes;                   // [chunk][128 scales]
+    static constexpr int STAGE = (X_BYTES + W_BYTES + S_BYTES + 1023) / 1024 * 1024;
     static constexpr int ACCS = TOK <= 128 ? 2 : 1;                   // TMEM accumulator buffers
     static constexpr int A_COL0 = ACCS * TOK;                         // first A-ring column
-    static constexpr int A_STAGES = (512 - A_COL0) / 32 < 8 ? (512 - A_COL0) / 32 : 8;
+    static constexpr int A_COLS = 32 * KCH;                           // TMEM columns of one A slot
+    static constexpr int A_STAGES = (512 - A_COL0) / A_COLS < 8 ? (512 - A_COL0) / A_COLS : 8;
     static constexpr int BAR_BYTES = 1024;
     static constexpr int ST_FIT = (kPfSmemBudget - 1024 - BAR_BYTES) / STAGE;
     static constexpr int STAGES = ST_FIT < 12 ? ST_FIT : 12;
@@ -77,7 +96,7 @@ struct PfCfg {
     // Request > half of the SM's shared memory so at most one CTA (which owns all
     // 512 TMEM columns) is ever resident on an SM.
     static constexpr int SMEM = SMEM_USED > 116 * 1024 ? SMEM_USED : 116 * 1024;
-    static_assert(A_COL0 + A_STAGES * 32 <= 512, "TMEM budget");
+    static_assert(A_COL0 + A_STAGES * A_COLS <= 512 && A_STAGES >= 2, "TMEM budget");
     static_assert(STAGES >= 3, "pipeline depth");
 };
 
@@ -154,7 +173,9 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
 
     const int n_tiles = (N + kPfRows - 1) / kPfRows;
     const int total = n_tiles * ((M + TOK - 1) / TOK);
-    const int KT = K >> 6;
+    const int KC = K >> 6;                                  // 64-wide K chunks
+    const int KB = KC < C::KCH ? KC : C::KCH;               // chunks in a stage's weight box
+    const int KT = (KC + C::KCH - 1) / C::KCH;              // stages per tile
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
@@ -166,11 +187,18 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 for (int kt = 0; kt < KT; ++kt, ++it) {
                     const int s = it % ST;
                     if (!mbar_wait(empty(s), ((it / ST) & 1) ^ 1, kDevTimeoutPipeline)) { ok = false; break; }
+                    // the stage's chunks c0 .. c0 + nch - 1: one x tile and one scale row per
+                    // chunk, the packed words of all of them in one box (a last partial stage's
+                    // box runs past K and reads zeros)
                     const uint32_t sb = base + s * C::STAGE;
-                    mbar_arrive_expect_tx(full(s), C::X_BYTES + kPfWBytes + kPfSBytes);
-                    tma_load_2d(sb, &tm_x, kt * 64, tt * TOK, full(s));
-                    tma_load_3d(sb + C::X_BYTES, &tm_w, 0, kt, tn * 8, full(s));
-                    tma_load_2d(sb + C::X_BYTES + kPfWBytes, &tm_s, tn * kPfRows, (kt * 64) / G, full(s));
+                    const int c0 = kt * C::KCH, nch = KC - c0 < C::KCH ? KC - c0 : C::KCH;
+                    mbar_arrive_expect_tx(full(s), (uint32_t)(nch * (C::X_CHUNK + kPfSBytes) + KB * kPfWBytes));
+                    for (int j = 0; j < nch; ++j)
+                        tma_load_2d(sb + j * C::X_CHUNK, &tm_x, (c0 + j) * 64, tt * TOK, full(s));
+                    tma_load_3d(sb + C::X_BYTES, &tm_w, 0, c0, tn * 8, full(s));
+                    for (int j = 0; j < nch; ++j)
+                        tma_load_2d(sb + C::X_BYTES + C::W_BYTES + j * kPfSBytes, &tm_s, tn * kPfRows,
+                                    ((c0 + j) * 64) / G, full(s));
                 }
             }
             if (!ok) {
@@ -196,10 +224,13 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                         !mbar_wait(afull(a), (it / NA) & 1, kDevTimeoutPipeline)) { ok = false; break; }
                     tc_fence_after();
                     const uint32_t xa = base + s * C::STAGE;
-                    const uint32_t at = tmem + (uint32_t)(C::A_COL0 + a * 32);
+                    const uint32_t at = tmem + (uint32_t)(C::A_COL0 + a * C::A_COLS);
+                    const int nch = KC - kt * C::KCH < C::KCH ? KC - kt * C::KCH : C::KCH;
+                    for (int j = 0; j < nch; ++j)
 #pragma unroll
-                    for (int k16 = 0; k16 < 4; ++k16)
-                        tc_mma_ts(d, at + k16 * 8, pf_sw128_desc(xa + k16 * 32), idesc, (kt | k16) != 0);
+                        for (int k16 = 0; k16 < 4; ++k16)
+                            tc_mma_ts(d, at + j * 32 + k16 * 8, pf_sw128_desc(xa + j * C::X_CHUNK + k16 * 32), idesc,
+                                      (kt | j | k16) != 0);
                     tc_commit(empty(s));
                     tc_commit(aempty(a));
                 }
@@ -225,18 +256,31 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 w_ok = w_ok && mbar_wait(aempty(a), ((it / NA) & 1) ^ 1, kDevTimeoutPipeline);
                 if (!__all_sync(0xffffffffu, w_ok)) { ok = false; break; }
                 tc_fence_after();
-                const uint32_t sb = base + s * C::STAGE + C::X_BYTES;
-                const uint4 w = lds128(sb + nbl * 512 + lane * 16);
-                const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem_raw + (sb + kPfWBytes - raw));
-                const uint32_t s_lo = bcast_half(sc[nbl * 16 + g]);
-                const uint32_t s_hi = bcast_half(sc[nbl * 16 + g + 8]);
-                uint32_t r[16];
-                dequant_word(w.x, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[0]));
-                dequant_word(w.y, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[4]));
-                dequant_word(w.z, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[8]));
-                dequant_word(w.w, s_lo, s_hi, *reinterpret_cast<uint32_t(*)[4]>(&r[12]));
+                // this warp's block of every chunk of the stage: words [block][chunk][512 B],
+                // scales [chunk][128]; all read before the stage is released
+                const int nch = KC - kt * C::KCH < C::KCH ? KC - kt * C::KCH : C::KCH;
+                const uint32_t sbw = base + s * C::STAGE + C::X_BYTES, sbs = sbw + C::W_BYTES;
+                uint4 w[C::KCH];
+                uint32_t s_lo[C::KCH], s_hi[C::KCH];
+#pragma unroll
+                for (int j = 0; j < C::KCH; ++j)
+                    if (j < nch) {
+                        w[j] = lds128(sbw + (uint32_t)((nbl * KB + j) * 512 + lane * 16));
+                        const uint16_t* sc = reinterpret_cast<const uint16_t*>(smem_raw + (sbs + j * kPfSBytes - raw));
+                        s_lo[j] = bcast_half(sc[nbl * 16 + g]);
+                        s_hi[j] = bcast_half(sc[nbl * 16 + g + 8]);
+                    }
                 mbar_arrive(empty(s));   // this lane is done with the stage's packed words and scales
-                tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * 32), r);
+                uint32_t r[C::KCH][16];   // one register set per chunk: no store's sources are reused
+#pragma unroll
+                for (int j = 0; j < C::KCH; ++j)
+                    if (j < nch) {
+                        dequant_word(w[j].x, s_lo[j], s_hi[j], *reinterpret_cast<uint32_t(*)[4]>(&r[j][0]));
+                        dequant_word(w[j].y, s_lo[j], s_hi[j], *reinterpret_cast<uint32_t(*)[4]>(&r[j][4]));
+                        dequant_word(w[j].z, s_lo[j], s_hi[j], *reinterpret_cast<uint32_t(*)[4]>(&r[j][8]));
+                        dequant_word(w[j].w, s_lo[j], s_hi[j], *reinterpret_cast<uint32_t(*)[4]>(&r[j][12]));
+                        tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * C::A_COLS + j * 32), r[j]);
+                    }
                 tc_wait_st();
                 tc_fence_before();
                 mbar_arrive(afull(a));
@@ -356,7 +400,7 @@ PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInf
 }
 
 // Tensor maps for one call.  x: [M, K] fp16, box {64, TOK}, 128-byte swizzle.
-// Packed words as [NB][KC][128] int32, box {128, 1, 8} (8 n16 blocks of one chunk).
+// Packed words as [NB][KC][128] int32, box {128, min(pf_kch(TOK), KC), 8} (8 n16 blocks of a stage).
 // Scales: [K/G, N] fp16, box {128, 1}.  Out-of-range boxes read as zero.
 cudaError_t make_prefill_tensor_maps(const GemmArgs& a, int tok, CUtensorMap* tx, CUtensorMap* tw, CUtensorMap* ts);
 
