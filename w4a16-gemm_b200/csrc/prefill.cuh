@@ -371,18 +371,19 @@ PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInf
     (void)K; (void)G;
     const int n_tiles = (N + kPfRows - 1) / kPfRows;
     if (config < 1 || config > 4) {
-        // Wave-quantised cost of a tile.  A k-step always dequantises a fixed 128 x 64
-        // weight tile, which on B200 costs about as much as the MMA of a 200-token tile
-        // (measured: a 128-token tile takes ~0.79x the time of a 256-token one), so below
-        // that the dequant, not the MMA, sets the pace.
-        double best = 1e300;
-        config = 3;
-        for (int c = 4; c >= 1; --c) {
+        // Fewest waves of tiles over the SMs; among equal wave counts the smallest token tile.
+        // Measured on B200 (design notes, prefill section): below one wave a smaller tile
+        // spreads the same weights over more SMs and takes more K chunks per stage (4 for 32-
+        // and 64-token tiles, 3 for 128), e.g. M = 128 x 4096 x 14336 in 58.7 us with 32-token
+        // tiles against 65.8 with 128; once tiles fill the SMs, a 256-token tile dequantises
+        // each weight tile once for twice the tokens.
+        long long best = -1;
+        config = 4;
+        for (int c = 1; c <= 4; ++c) {
             const int tok = pf_tok_of_config(c);
-            const double tiles = (double)n_tiles * ((M + tok - 1) / tok);
-            const double waves = std::ceil(tiles / dev.num_sms);
-            const double cost = waves * std::max(tok, 200);
-            if (cost < best - 1e-9) { best = cost; config = c; }
+            const long long tiles = (long long)n_tiles * ((M + tok - 1) / tok);
+            const long long waves = (tiles + dev.num_sms - 1) / dev.num_sms;
+            if (best < 0 || waves < best) { best = waves; config = c; }
         }
     }
     PrefillPlan p;
