@@ -3,7 +3,7 @@
 The counterpart, for this package's tcgen05 prefill kernel, of the reference's numpy
 emulation of its own prefill kernel (akshay919191/W4A16-GEMM tests/layout_prefill.py).
 One CTA walks every (token tile, 128-row tile) and every pipeline stage as prefill_kernel
-does (csrc/prefill.cuh); a stage holds KCH 64-wide K chunks (KCH = pf_kch(TOK): 4, 4, 3, 2
+does (csrc/prefill.cuh); a stage holds KCH 64-wide K chunks (KCH = pf_kch(TOK): 6, 6, 3, 2
 for 32, 64, 128, 256-token tiles; a last stage may hold fewer):
 
 * Dequant warps 2..9 each take n16 block `nbl = 2 (warp & 3) + (qi & 1)` of every chunk's
@@ -39,7 +39,7 @@ ROWS, DQ_WARP0, DQ_WARPS, EPI_WARP0, EPI_WARPS = 128, 2, 8, 10, 16
 
 
 def pf_kch(TOK):
-    return 4 if TOK <= 64 else 3 if TOK == 128 else 2
+    return 6 if TOK <= 64 else 3 if TOK == 128 else 2
 
 
 def cfg(TOK):
@@ -150,9 +150,9 @@ def emulate(Wp, x, scales, N, K, G, TOK):
 
 CASES = [
     # M, N, K, G, TOK: ragged M and N, every token tile, both group sizes; stages of
-    # 4 + 2, 4, 3 + 1 and 2 + 1 chunks (a last partial stage), one chunk only
+    # 6, 6 + 2, 3 + 1 and 2 + 1 chunks (a last partial stage), one chunk only
     (17, 208, 384, 64, 32),
-    (100, 272, 256, 128, 64),
+    (100, 272, 512, 128, 64),
     (129, 128, 256, 64, 128),
     (40, 384, 320, 64, 256),
     (20, 144, 64, 64, 128),

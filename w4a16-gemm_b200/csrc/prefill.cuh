@@ -66,7 +66,7 @@ constexpr int kPfSBytes = kPfRows * 2;       // one fp16 scale row slice
 // fewer trips per K.  The chunks are still multiplied in K order, one k16 step at a time.
 // Per token tile: as many as keep at least 3 stages in shared memory and 2 A slots in TMEM.
 #ifndef W4A16_PF_KCH_SMALL
-#define W4A16_PF_KCH_SMALL 4
+#define W4A16_PF_KCH_SMALL 6
 #endif
 #ifndef W4A16_PF_KCH_128
 #define W4A16_PF_KCH_128 3
@@ -373,8 +373,8 @@ PrefillPlan plan_prefill(int M, int N, int K, int G, int config, const DeviceInf
     if (config < 1 || config > 4) {
         // Fewest waves of tiles over the SMs; among equal wave counts the smallest token tile.
         // Measured on B200 (design notes, prefill section): below one wave a smaller tile
-        // spreads the same weights over more SMs and takes more K chunks per stage (4 for 32-
-        // and 64-token tiles, 3 for 128), e.g. M = 128 x 4096 x 14336 in 58.7 us with 32-token
+        // spreads the same weights over more SMs and takes more K chunks per stage (6 for 32-
+        // and 64-token tiles, 3 for 128), e.g. M = 128 x 4096 x 14336 in 55-59 us with 32-token
         // tiles against 65.8 with 128; once tiles fill the SMs, a 256-token tile dequantises
         // each weight tile once for twice the tokens.
         long long best = -1;
