@@ -16,8 +16,9 @@ for 32, 64, 128, 256-token tiles; a last stage may hold fewer):
   advanced by 32 bytes per slice. It accumulates into columns b * TOK of the fp32
   accumulator, overwriting on the first slice of a tile, in K order.
 * Epilogue warp (quarter q = warp & 3, part h) reads TMEM lanes 32q..32q+31 and token
-  columns h * TOK/4 .. (h + 1) * TOK/4 - 1 and stores row n = 128 tn + 32q + lane,
-  tokens TOK tt + h * TOK/4 + j, guarded by N and M.
+  columns h * TOK/4 .. (h + 1) * TOK/4 - 1 (channel n = 128 tn + 32q + lane); lanes 2i and
+  2i + 1 trade halves, and the even lane stores token j, the odd lane token j + 1, each as
+  one 4-byte pair of channels (n0, n0 + 1), guarded by N and M.
 
 Hardware facts assumed, from the PTX ISA:
 * tcgen05.st .16x128b: thread T's register 2j goes to lane T/4, column 4j + T%4, and
@@ -131,19 +132,26 @@ def emulate(Wp, x, scales, N, K, G, TOK):
                     B = xts[j][:, k16 * 16:(k16 + 1) * 16].T        # [16 k, TOK]
                     D = tmem[:, b * TOK:(b + 1) * TOK, 0]
                     tmem[:, b * TOK:(b + 1) * TOK, 0] = A @ B + (D if (kt | j | k16) != 0 else 0.0)
-        # epilogue warps
+        # epilogue warps: each lane loads its channel's tokens; lanes 2i and 2i + 1 then trade
+        # halves, the even lane storing token j and the odd lane token j + 1 of both channels
         cw = TOK // (EPI_WARPS // 4)
         for warp in range(EPI_WARP0, EPI_WARP0 + EPI_WARPS):
             q, h = warp & 3, (warp - EPI_WARP0) >> 2
+            vals = np.zeros((32, cw))
             for L in range(32):
                 lane = 32 * q + L
                 check_lane(warp, lane)
-                n = tn * ROWS + 32 * q + L
-                tok0 = tt * TOK + h * cw
-                for j in range(cw):
-                    if n < N and tok0 + j < M:
-                        y[tok0 + j, n] = tmem[lane, b * TOK + h * cw + j, 0]
-                        written[tok0 + j, n] += 1
+                vals[L] = tmem[lane, b * TOK + h * cw:b * TOK + (h + 1) * cw, 0]
+            tok0 = tt * TOK + h * cw
+            for L in range(32):
+                p = L & 1
+                n0 = tn * ROWS + 32 * q + L - p            # the pair's even channel
+                for j in range(0, cw, 2):
+                    row = tok0 + j + p
+                    if n0 < N and row < M:
+                        for c in range(2):                  # channels n0, n0 + 1 of one 4-byte store
+                            y[row, n0 + c] = vals[L - p + c, j + p]
+                            written[row, n0 + c] += 1
     assert (written == 1).all(), "y elements written zero or several times"
     return y
 
@@ -192,5 +200,8 @@ def test_emulation_constants_match_kernel_sources():
     assert "const int nbl = 2 * (warp & 3) + (qi & 1);" in src
     assert "tmem_st_16x128b_x8(tmem + lane_field + (uint32_t)(C::A_COL0 + a * C::A_COLS + j * 32), r[j]);" in src
     assert "w[j] = lds128(sbw + (uint32_t)((nbl * KB + j) * 512 + lane * 16));" in src
+    assert "uint32_t* y32 = reinterpret_cast<uint32_t*>(static_cast<__half*>(yv) + (size_t)(tok0 + p) * N + n0);" in src
+    assert "const uint32_t out = p ? __byte_perm(got, w, 0x7610) : __byte_perm(w, got, 0x5410);" in src
+    assert "if (n0 < N && tok0 + j + p < M) y32[(size_t)j * N / 2] = out;" in src
     assert ("tc_mma_ts(d, at + j * 32 + k16 * 8, pf_sw128_desc(xa + j * C::X_CHUNK + k16 * 32), idesc,\n"
             "                                      (kt | j | k16) != 0);") in src

@@ -336,16 +336,20 @@ prefill_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__
                 }
                 tc_fence_before();
                 mbar_arrive(accempty(b));
-                if (n < N) {
-                    const int jmax = min(CW, M - tok0);
-                    __half* y = static_cast<__half*>(yv) + (size_t)tok0 * N + n;
+                // lanes 2i and 2i+1 (channels n0, n0 + 1) trade halves so that the even lane
+                // stores tokens j and the odd lane tokens j + 1 as fp16 pairs of both channels
+                {
+                    const int p = lane & 1;
+                    const int n0 = n - p;
+                    uint32_t* y32 = reinterpret_cast<uint32_t*>(static_cast<__half*>(yv) + (size_t)(tok0 + p) * N + n0);
 #pragma unroll
-                    for (int j = 0; j < CW; ++j)
-                        if (j < jmax) {
-                            const uint32_t w = hv[j / 2];
-                            const uint16_t bits = (j & 1) ? (uint16_t)(w >> 16) : (uint16_t)(w & 0xFFFF);
-                            y[(size_t)j * N] = *reinterpret_cast<const __half*>(&bits);
-                        }
+                    for (int j = 0; j < CW; j += 2) {
+                        const uint32_t w = hv[j / 2];
+                        const uint32_t give = p ? w : (w >> 16);          // partner's token of the pair
+                        const uint32_t got = __shfl_xor_sync(0xffffffffu, give, 1);
+                        const uint32_t out = p ? __byte_perm(got, w, 0x7610) : __byte_perm(w, got, 0x5410);
+                        if (n0 < N && tok0 + j + p < M) y32[(size_t)j * N / 2] = out;
+                    }
                 }
             }
         }
