@@ -48,7 +48,7 @@
 extern "C" {
 #endif
 
-#define W4A16_ABI_VERSION 3
+#define W4A16_ABI_VERSION 4
 
 /* Size of the scratch array built into the library for w4a16_gemm_noalloc
  * (6 MiB per device: the decode path's partials on a GPU of up to 192 SMs). */
@@ -213,6 +213,9 @@ w4a16_status w4a16_quantize_pack(const void* W, int32_t w_dtype, int32_t* Wp, vo
  * w4a16_device_status) and the kernel returns instead of hanging. */
 #define W4A16_TP_MAX_RANKS 8
 #define W4A16_TP_CTRL_BYTES 8192u
+/* Largest per-rank contribution (bytes) that an exchange sends in one round (see
+ * w4a16_tp_group.recv_off). */
+#define W4A16_TP_PUSH_MAX_BYTES (1u << 20)
 
 typedef struct w4a16_ipc_handle {
     unsigned char bytes[64];   /* a cudaIpcMemHandle_t */
@@ -223,6 +226,15 @@ typedef struct w4a16_tp_group {
     int32_t world;                         /* ranks, 1 .. W4A16_TP_MAX_RANKS */
     void* buf[W4A16_TP_MAX_RANKS];         /* every rank's exchange buffer as mapped here (buf[rank]: own) */
     uint64_t buf_bytes;                    /* size of each buffer */
+    /* Optional receive area in every buffer (recv_bytes 0: none).  An exchange whose per-rank
+     * contribution c (allgather: M * N / world * 2 bytes, allreduce: M * N * 4 bytes) is at
+     * most W4A16_TP_PUSH_MAX_BYTES and fits 2 * world slots of c bytes (rounded up to 256)
+     * here runs in one round: every rank stores its contribution into its slot of every
+     * peer's receive area and raises one flag, and each rank builds its y from the slots.
+     * Other exchanges run in two rounds (a ready flag, then loads from the peers' source
+     * regions).  Results are the same either way. */
+    uint64_t recv_off;
+    uint64_t recv_bytes;
 } w4a16_tp_group;
 
 /* Allocates a zero-filled exchange buffer of `bytes` on the current device and its IPC

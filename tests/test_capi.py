@@ -28,7 +28,7 @@ def test_library_loads_and_exports_every_symbol():
     lib = capi.load()
     for name in declared_functions():
         assert hasattr(lib, name), name
-    assert lib.w4a16_abi_version() == 3
+    assert lib.w4a16_abi_version() == 4
 
 
 def test_library_has_no_torch_dependency():
@@ -129,7 +129,7 @@ def test_binding_exports():
     import w4a16_opt
     for name in ("w4a16_gemm", "w4a16_gemm_out", "w4a16_dequant", "query_route", "device_status"):
         assert callable(getattr(w4a16_opt, name))
-    assert w4a16_opt.ABI_VERSION == 3
+    assert w4a16_opt.ABI_VERSION == 4
 
 
 @pytest.mark.skipif(__import__("shutil").which("gcc") is None, reason="needs gcc")
@@ -142,6 +142,9 @@ def test_header_layout_matches_ctypes(tmp_path):
     lines = ["#include <stddef.h>", "#include <stdio.h>", '#include "w4a16.h"', "int main(void) {",
              '    printf("sizeof %zu\\n", sizeof(w4a16_route));']
     lines += [f'    printf("{f} %zu\\n", offsetof(w4a16_route, {f}));' for f in fields]
+    tp_fields = [name for name, _ in capi.TpGroup._fields_]
+    lines += ['    printf("tp_sizeof %zu\\n", sizeof(w4a16_tp_group));']
+    lines += [f'    printf("tp_{f} %zu\\n", offsetof(w4a16_tp_group, {f}));' for f in tp_fields]
     lines += [f'    printf("{name} %d\\n", (int){name});' for name in capi.STATUS_NAMES.values()]
     lines += ['    printf("W4A16_FLAG_WEIGHTS_RESIDENT %d\\n", (int)W4A16_FLAG_WEIGHTS_RESIDENT);',
               '    printf("W4A16_FLAG_FP32_SCALE %d\\n", (int)W4A16_FLAG_FP32_SCALE);']
@@ -154,6 +157,9 @@ def test_header_layout_matches_ctypes(tmp_path):
     out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True, text=True,
                                                        check=True).stdout.splitlines())
     assert int(out["sizeof"]) == ctypes.sizeof(capi.Route)
+    assert int(out["tp_sizeof"]) == ctypes.sizeof(capi.TpGroup)
+    for f in tp_fields:
+        assert int(out["tp_" + f]) == getattr(capi.TpGroup, f).offset, f
     for f in fields:
         assert int(out[f]) == getattr(capi.Route, f).offset, f
     for code, name in capi.STATUS_NAMES.items():

@@ -1,8 +1,10 @@
 """The tensor-parallel exchange (csrc/tp_exchange.cuh) checked on the CPU.
 
-* A thread-per-(rank, CTA) emulation of the exchange kernel's protocol -- ready flags,
-  per-CTA done flags, per-CTA epochs, waits that accept a flag at or past the expected
-  epoch -- over shared arrays that stand in for the ranks' buffers.  Random delays move the
+* A thread-per-(rank, CTA) emulation of the exchange kernels' protocols -- the two-round
+  pull (ready flags, per-CTA done flags) and the one-round push (contributions stored into
+  parity slots of every peer's receive area, one per-CTA done flag), per-CTA epochs, waits
+  that accept a flag at or past the expected epoch -- over shared arrays that stand in for
+  the ranks' buffers; calls of both protocols interleave as the C ABI chooses them by size.  Random delays move the
   threads of different ranks and calls past one another; every call must still produce the
   rank-order sum (reduce) or the column gather, on every rank.  A rank that stops joining
   (a stalled peer, injected on the host) must make the others' bounded waits end in an
@@ -33,6 +35,9 @@ class Exchange:
         self.done = np.zeros((world, world, CTAS), np.int64)     # [buffer][src][cta]
         self.epoch = np.zeros((world, CTAS), np.int64)           # [rank][cta]
         self.y = np.full((world, M, N), np.nan)
+        # receive area: [buffer][parity][src] one contribution each (stale values start as NaN)
+        shape = (M, N // world) if gather else (M, N)
+        self.recv = np.full((world, 2, world) + shape, np.nan, np.float16 if gather else np.float32)
         self.lock = threading.Lock()
 
     def wait_at_least(self, get, e):
@@ -44,6 +49,44 @@ class Exchange:
             if time.monotonic() - t0 > self.limit:
                 raise PeerTimeout()
             time.sleep(0.0005 * random.random())
+
+    def push_cta(self, rank, cta, src_regions):
+        """One CTA of tp_push_kernel on `rank`: send this CTA's units of the contribution to
+        slot (e & 1, rank) of every peer, one flag per peer, wait for CTA cta of every peer,
+        build y from the own source region and the received slots."""
+        W, M, N = self.world, self.M, self.N
+        e = self.epoch[rank, cta] + 1
+        par = e & 1
+        own = src_regions[rank]
+        flat = own.reshape(-1)
+        units = flat.size // (8 if self.gather else 4)                 # 16-byte units
+        per = 8 if self.gather else 4
+        lo, hi = units * cta // CTAS * per, units * (cta + 1) // CTAS * per
+        for t in range(W):                                             # A: stores into every peer
+            if t != rank:
+                self.recv[t, par, rank].reshape(-1)[lo:hi] = flat[lo:hi]
+                time.sleep(0.0002 * random.random())
+        with self.lock:                                                # B: flags, then wait
+            for t in range(W):
+                if t != rank:
+                    self.done[t, rank, cta] = max(self.done[t, rank, cta], e)
+        for src in range(W):
+            if src != rank:
+                self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
+        # C: y from the same units
+        if self.gather:
+            nl = N // W
+            for src in range(W):
+                part = (own if src == rank else self.recv[rank, par, src]).reshape(-1)[lo:hi]
+                for i, v in zip(range(lo, hi), part):
+                    m, c = divmod(i, nl)
+                    self.y[rank, m, src * nl + c] = np.float16(v)
+        else:
+            acc = np.zeros(hi - lo, np.float32)
+            for src in range(W):                                       # rank order
+                acc = acc + (own if src == rank else self.recv[rank, par, src]).reshape(-1)[lo:hi]
+            self.y[rank].reshape(-1)[lo:hi] = np.float16(acc)
+        self.epoch[rank, cta] = e
 
     def cta(self, rank, cta, src_regions):
         """One CTA of the exchange kernel on `rank` (phases A, B, C); src_regions[r] is rank
@@ -77,7 +120,7 @@ class Exchange:
         self.epoch[rank, cta] = e
 
 
-def run_calls(ex, inputs, stall_rank=None, stall_call=None):
+def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=()):
     """Every rank issues the calls in order, with no host synchronisation between ranks (a
     fast rank runs ahead); each call's CTAs run as threads.  After each call a rank reads its
     own y: no peer may write the next call's results into it before this rank announced
@@ -89,7 +132,7 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None):
         for i, src in enumerate(inputs):
             if rank == stall_rank and i == stall_call:
                 return                                            # stops joining: never starts call i
-            threads = [threading.Thread(target=_cta, args=(rank, c, src)) for c in range(CTAS)]
+            threads = [threading.Thread(target=_cta, args=(rank, c, src, i in push)) for c in range(CTAS)]
             for t in threads:
                 t.start()
             for t in threads:
@@ -98,9 +141,9 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None):
                 return
             results[rank].append(ex.y[rank].copy())
 
-    def _cta(rank, c, src):
+    def _cta(rank, c, src, one_round):
         try:
-            ex.cta(rank, c, src)
+            (ex.push_cta if one_round else ex.cta)(rank, c, src)
         except Exception as exc:                                  # noqa: BLE001
             errors.append(exc)
 
@@ -115,19 +158,22 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None):
     return results
 
 
+@pytest.mark.parametrize("mix", ["pull", "push", "mixed"])
 @pytest.mark.parametrize("world", [2, 3, 4])
 @pytest.mark.parametrize("gather", [False, True])
-def test_exchange_protocol_results(world, gather):
+def test_exchange_protocol_results(world, gather, mix):
     rng = np.random.default_rng(world)
     M, N = 3, 16 * world
+    calls = 10
+    push = {"pull": (), "push": tuple(range(calls)), "mixed": (1, 2, 4, 7, 8)}[mix]
     inputs = []
-    for _ in range(4):
+    for _ in range(calls):
         if gather:
             inputs.append([rng.standard_normal((M, N // world)).astype(np.float16) for _ in range(world)])
         else:
             inputs.append([rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)])
     ex = Exchange(world, M, N, gather)
-    results = run_calls(ex, inputs)
+    results = run_calls(ex, inputs, push=push)
     assert all(len(r) == len(inputs) for r in results)
     for i, src in enumerate(inputs):
         if gather:
@@ -142,14 +188,15 @@ def test_exchange_protocol_results(world, gather):
     assert (ex.epoch == len(inputs)).all()
 
 
-def test_stalled_peer_is_an_error_not_a_hang():
+@pytest.mark.parametrize("push", [(), (0, 1, 2)])
+def test_stalled_peer_is_an_error_not_a_hang(push):
     world, M, N = 3, 2, 48
     rng = np.random.default_rng(0)
     inputs = [[rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)] for _ in range(3)]
     ex = Exchange(world, M, N, gather=False, limit_s=0.5)
     t0 = time.monotonic()
     with pytest.raises(PeerTimeout):
-        run_calls(ex, inputs, stall_rank=2, stall_call=1)
+        run_calls(ex, inputs, stall_rank=2, stall_call=1, push=push)
     assert time.monotonic() - t0 < 30
 
 
@@ -186,6 +233,21 @@ def test_exchange_rejects_bad_regions(args, msg):
     lib = capi.load()
     g = _group(capi)
     st = lib.w4a16_tp_allreduce(ctypes.byref(g), *args, None)
+    assert st != 0 and msg in capi.last_error(lib)
+
+
+@pytest.mark.parametrize("recv,msg", [
+    ((8192 + 16, 4096), "256-byte boundary"),
+    ((4096, 4096), "past the flags"),
+    (((1 << 20) - 2048, 4096), "inside the buffers"),
+    ((1 << 19, 4096), "must not overlap"),
+])
+def test_exchange_rejects_bad_receive_areas(recv, msg):
+    from w4a16_opt import capi
+    lib = capi.load()
+    g = _group(capi)
+    g.recv_off, g.recv_bytes = recv
+    st = lib.w4a16_tp_allreduce(ctypes.byref(g), 8192, 1 << 19, 2, 64, None)
     assert st != 0 and msg in capi.last_error(lib)
 
 

@@ -1,7 +1,8 @@
-"""The tensor-parallel exchange kernel on one GPU, through the C ABI.
+"""The tensor-parallel exchange kernels on one GPU, through the C ABI.
 
 * A one-rank group: the reduction is a cast of the rank's fp32 partial to fp16 and the
-  gather a copy, over several calls (the per-CTA epochs advance).
+  gather a copy, over several calls (the per-CTA epochs advance), in the two-round form
+  (no receive area) and the one-round form (a receive area).
 * A bounded wait that runs out: a two-rank group whose second buffer is memory of this GPU
   that no rank ever flags.  The kernel must give up after its wait limit (about 2 s),
   record kDevTimeoutPeer (7) in the device status word and return, leaving the context
@@ -28,14 +29,17 @@ def _view(ptr, shape, dtype):
     return torch.as_tensor(_CudaRegion(ptr, shape, typestr), device="cuda")
 
 
-def test_one_rank_exchange(cuda_device):
+@pytest.mark.parametrize("one_round", [False, True])
+def test_one_rank_exchange(one_round, cuda_device):
     from w4a16_opt import capi
     lib = capi.load()
     M, N = 16, 4096
     src_off, y_off = capi.TP_CTRL_BYTES, capi.TP_CTRL_BYTES + M * N * 4
-    nbytes = y_off + M * N * 2
+    recv_off = y_off + M * N * 2
+    recv_bytes = 2 * M * N * 4 if one_round else 0
+    nbytes = recv_off + recv_bytes
     buf = _alloc(lib, capi, nbytes)
-    g = capi.TpGroup(0, 1, (ctypes.c_void_p * capi.TP_MAX_RANKS)(buf), nbytes)
+    g = capi.TpGroup(0, 1, (ctypes.c_void_p * capi.TP_MAX_RANKS)(buf), nbytes, recv_off, recv_bytes)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     try:
         for i in range(3):
@@ -54,16 +58,19 @@ def test_one_rank_exchange(cuda_device):
         capi.check(lib.w4a16_peer_free(ctypes.c_void_p(buf)), lib)
 
 
-def test_peer_that_never_arrives_times_out(cuda_device):
+@pytest.mark.parametrize("one_round", [False, True])
+def test_peer_that_never_arrives_times_out(one_round, cuda_device):
     from w4a16_opt import capi, device_status
     lib = capi.load()
     M, N = 1, 256
     src_off, y_off = capi.TP_CTRL_BYTES, capi.TP_CTRL_BYTES + M * N * 4
-    nbytes = y_off + M * N * 2
+    recv_off = y_off + M * N * 2
+    recv_bytes = 2 * 2 * M * N * 4 if one_round else 0
+    nbytes = recv_off + recv_bytes
     assert device_status(reset=True) == 0
     bufs = [_alloc(lib, capi, nbytes) for _ in range(2)]
     # rank 0 of two; "rank 1" is a buffer of this GPU that no kernel ever flags
-    g = capi.TpGroup(0, 2, (ctypes.c_void_p * capi.TP_MAX_RANKS)(*bufs), nbytes)
+    g = capi.TpGroup(0, 2, (ctypes.c_void_p * capi.TP_MAX_RANKS)(*bufs), nbytes, recv_off, recv_bytes)
     try:
         t0 = time.monotonic()
         capi.check(lib.w4a16_tp_allreduce(ctypes.byref(g), src_off, y_off, M, N,

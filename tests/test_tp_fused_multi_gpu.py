@@ -4,7 +4,8 @@ Two child processes, one per GPU, NCCL for set-up (handles, barriers) and for th
 reference path.  For the column-parallel (N split, gather) and row-parallel (K split, fp32
 reduction) layers at decode and prefill batch sizes:
 * the fused path (GEMM into the exchange buffer + the library's exchange kernel) matches
-  the CPU oracle within the tests' tolerance;
+  the CPU oracle within the tests' tolerance, with the one-round exchange (receive area)
+  and the two-round one (none), which give the same bits;
 * it gives bitwise identical y on both ranks (every rank holds the same rank-order sums);
 * it matches the NCCL path (all_gather_into_tensor / all_reduce) within tolerance -- the
   reduction order of NCCL's all-reduce is its own, so not bit for bit.
@@ -43,7 +44,9 @@ def _rank_main(rank, port, out):
     dist.init_process_group("nccl", rank=rank, world_size=WORLD, timeout=datetime.timedelta(seconds=60),
                             device_id=torch.device("cuda", rank))
     res = {}
-    ex = tp.PeerExchange(src_bytes=max(M * N * 4 for M, N, _ in CASES), y_bytes=max(M * N * 2 for M, N, _ in CASES))
+    sb, yb = max(M * N * 4 for M, N, _ in CASES), max(M * N * 2 for M, N, _ in CASES)
+    ex = tp.PeerExchange(src_bytes=sb, y_bytes=yb)                    # one round at these sizes
+    ex2 = tp.PeerExchange(src_bytes=sb, y_bytes=yb, push_bytes=0)     # always two rounds
     try:
         for M, N, K in CASES:
             x, q, s, Wp = make_workload(M, N, K, 128, seed=M + N + K)
@@ -51,12 +54,17 @@ def _rank_main(rank, port, out):
             row = tp.RowParallelW4A16(Wp, s, N, K, exchange=ex)
             y_col_f = col.fused(x).clone()
             y_row_f = row.fused(row.x_slice(x)).clone()
+            col.exchange = row.exchange = ex2
+            y_col_2 = col.fused(x).clone()
+            y_row_2 = row.fused(row.x_slice(x)).clone()
             y_col_n = col(x)
             y_row_n = row(row.x_slice(x))
             torch.cuda.synchronize()
-            res[(M, N, K)] = tuple(t.float().cpu().numpy() for t in (y_col_f, y_row_f, y_col_n, y_row_n))
+            res[(M, N, K)] = tuple(t.float().cpu().numpy() for t in (y_col_f, y_row_f, y_col_n, y_row_n,
+                                                                     y_col_2, y_row_2))
     finally:
         ex.close()
+        ex2.close()
         dist.destroy_process_group()
     out[rank] = res
 
@@ -83,9 +91,10 @@ def test_fused_exchange_two_gpus():
         x, q, s, _ = make_workload(M, N, K, 128, seed=M + N + K, device="cpu")
         ref = ref_gemm(x, q, s, 128)
         for rank in range(WORLD):
-            y_col_f, y_row_f, y_col_n, y_row_n = res[rank][(M, N, K)]
+            y_col_f, y_row_f, y_col_n, y_row_n, y_col_2, y_row_2 = res[rank][(M, N, K)]
             assert_close(y_col_f, ref)
             assert_close(y_row_f, ref)
+            assert np.array_equal(y_col_f, y_col_2) and np.array_equal(y_row_f, y_row_2)   # both protocols
             assert np.array_equal(y_col_f, y_col_n)           # the gather moves the same fp16 values
             assert_close(y_row_f, y_row_n.astype(np.float32))
         for k in range(2):

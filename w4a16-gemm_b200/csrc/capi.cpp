@@ -373,6 +373,14 @@ w4a16_status tp_check(const w4a16_tp_group* g, uint64_t src_off, uint64_t src_by
         return fail(W4A16_ERR_TP_GROUP, "exchange regions must lie past the flags and inside the buffers");
     if ((src_off < y_off + y_bytes) && (y_off < src_off + src_bytes))
         return fail(W4A16_ERR_TP_GROUP, "the source and result regions must not overlap");
+    if (g->recv_bytes > 0) {
+        if (g->recv_off % 256) return fail(W4A16_ERR_ALIGNMENT, "the receive area must start on a 256-byte boundary");
+        if (g->recv_off < w4a16::kTpCtrlBytes || g->recv_off + g->recv_bytes > g->buf_bytes)
+            return fail(W4A16_ERR_TP_GROUP, "the receive area must lie past the flags and inside the buffers");
+        if ((g->recv_off < y_off + y_bytes && y_off < g->recv_off + g->recv_bytes) ||
+            (g->recv_off < src_off + src_bytes && src_off < g->recv_off + g->recv_bytes))
+            return fail(W4A16_ERR_TP_GROUP, "the receive area must not overlap the source and result regions");
+    }
     for (int r = 0; r < g->world; ++r) {
         if (!g->buf[r]) return fail(W4A16_ERR_NULL_POINTER, "every rank's buffer must be mapped");
         if (reinterpret_cast<uintptr_t>(g->buf[r]) % 256) return fail(W4A16_ERR_ALIGNMENT, "buffers must be 256-byte aligned");
@@ -390,8 +398,11 @@ w4a16_status tp_launch(bool gather, const w4a16_tp_group* g, uint64_t src_off, u
     if (s != W4A16_OK) return s;
     w4a16::DeviceInfo d;
     if ((s = check_device(&d)) != W4A16_OK) return s;
-    const cudaError_t err = w4a16::launch_tp_exchange(gather, p, g->rank, g->world, src_off, y_off, (int)M, (int)N,
-                                                      static_cast<cudaStream_t>(stream));
+    // one round through the receive slots when the contribution is small and fits
+    const uint64_t slot = (src_bytes + 255) / 256 * 256;
+    const bool push = src_bytes <= W4A16_TP_PUSH_MAX_BYTES && g->recv_bytes >= 2ull * (uint64_t)g->world * slot;
+    const cudaError_t err = w4a16::launch_tp_exchange(gather, push, p, g->rank, g->world, src_off, y_off, g->recv_off,
+                                                      slot, (int)M, (int)N, static_cast<cudaStream_t>(stream));
     if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("kernel launch failed: ") + cudaGetErrorString(err));
     return ok();
 }

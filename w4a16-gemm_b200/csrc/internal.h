@@ -94,8 +94,11 @@ struct TpPtrs {
     char* buf[W4A16_TP_MAX_RANKS];   // every rank's exchange buffer as mapped in this process
 };
 constexpr size_t kTpCtrlBytes = W4A16_TP_CTRL_BYTES;
-cudaError_t launch_tp_exchange(bool gather, const TpPtrs& p, int rank, int world, uint64_t src_off, uint64_t y_off,
-                               int M, int N, cudaStream_t stream);
+// push: the one-round protocol through receive slots of slot_bytes at recv_off (2 * world
+// slots per buffer); otherwise the two-round pull from the peers' source regions.
+cudaError_t launch_tp_exchange(bool gather, bool push, const TpPtrs& p, int rank, int world, uint64_t src_off,
+                               uint64_t y_off, uint64_t recv_off, uint64_t slot_bytes, int M, int N,
+                               cudaStream_t stream);
 
 // ---------------------------------------------------------------- debug dequant
 cudaError_t launch_dequant(const void* wp, const void* scales, void* out, int N, int K, int G,

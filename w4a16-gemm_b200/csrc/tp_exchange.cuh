@@ -65,6 +65,13 @@ __device__ __forceinline__ float4 ld_relaxed_sys_f4(const float4* p) {
     return v;
 }
 
+__device__ __forceinline__ uint4 ld_relaxed_sys_u4(const uint4* p) {
+    uint4 v;
+    asm volatile("ld.relaxed.sys.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p) : "memory");
+    return v;
+}
+
 __device__ __forceinline__ void st_relaxed_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.relaxed.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
 }
@@ -192,8 +199,89 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
     if (tid == 0 && s_ok) *epoch = e;
 }
 
-cudaError_t launch_tp_exchange(bool gather, const TpPtrs& p, int rank, int world, uint64_t src_off, uint64_t y_off,
-                               int M, int N, cudaStream_t stream) {
+// One-round form for small contributions: call e (parity e & 1) of rank r stores its
+// contribution (gather: its fp16 columns [M, N/world]; reduce: its whole fp32 partial
+// [M, N]) into slot (e & 1, r) of every peer's receive area, raises done[r][cta] = e in every
+// peer's buffer after a system-scope fence, waits until every peer's CTA cta has done the
+// same, and builds its own y from its source region and the received slots: the gather
+// places each rank's columns, the reduction adds the ranks' partials in rank order.  Each
+// CTA sends and then reads the same range of 16-byte units of a contribution, so CTA cta's
+// flags cover exactly the units it reads.  A slot of parity p is written again two calls
+// later, after the writer has seen this rank's CTA cta finish the call in between, which
+// this rank's CTA cta starts only after it read the slot.  One fence per CTA and call (the
+// two-round form needs two; each costs microseconds at system scope).
+template <bool GATHER>
+__global__ void __launch_bounds__(kTpThreads) tp_push_kernel(const __grid_constant__ TpPtrs P, int rank, int world,
+                                                             uint64_t src_off, uint64_t y_off, uint64_t recv_off,
+                                                             uint64_t slot_bytes, int M, int N) {
+    __shared__ uint32_t s_e;
+    __shared__ int s_ok;
+    const int cta = blockIdx.x, tid = threadIdx.x;
+    char* const own = P.buf[rank];
+    uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff) + cta;
+    pdl_launch_dependents();
+    pdl_wait();   // the GEMM that wrote the source region has completed
+    if (tid == 0) {
+        s_e = *epoch + 1u;
+        s_ok = 1;
+    }
+    __syncthreads();
+    const uint32_t e = s_e;
+    const int nl = N / world;
+    const long long units = GATHER ? (long long)M * nl / 8 : (long long)M * N / 4;   // 16-byte units
+    const long long u0 = units * cta / gridDim.x, u1 = units * (cta + 1) / gridDim.x;
+    const uint64_t slot0 = recv_off + (uint64_t)(e & 1u) * (uint64_t)world * slot_bytes;   // this parity's slots
+    const uint4* const src = reinterpret_cast<const uint4*>(own + src_off);
+
+    // A. this CTA's units of the contribution into slot (parity, rank) of every peer
+    for (long long u = u0 + tid; u < u1; u += kTpThreads) {
+        const uint4 v = src[u];
+        for (int t = 0; t < world; ++t)
+            if (t != rank) reinterpret_cast<uint4*>(P.buf[t] + slot0 + (uint64_t)rank * slot_bytes)[u] = v;
+    }
+    __syncthreads();
+    // B. one flag per peer, after the CTA's stores; then wait for CTA cta of every peer
+    if (tid == 0) {
+        fence_acq_rel_sys();
+        for (int t = 0; t < world; ++t)
+            if (t != rank) st_relaxed_sys(reinterpret_cast<uint32_t*>(P.buf[t] + kTpDoneOff) + rank * kTpMaxCtas + cta, e);
+    }
+    if (tid < world && tid != rank &&
+        !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpDoneOff) + tid * kTpMaxCtas + cta, e))
+        s_ok = 0;
+    __syncthreads();
+    if (!s_ok) return;
+
+    // C. this rank's y from the same units: own source region and the received slots
+    for (long long u = u0 + tid; u < u1; u += kTpThreads) {
+        if (GATHER) {
+            const long long m = u / (nl / 8), c8 = (u % (nl / 8)) * 8;
+            for (int sr = 0; sr < world; ++sr) {
+                const uint4 v = sr == rank ? src[u]
+                                           : ld_relaxed_sys_u4(reinterpret_cast<const uint4*>(own + slot0 +
+                                                                                               (uint64_t)sr * slot_bytes) + u);
+                *reinterpret_cast<uint4*>(own + y_off + ((size_t)m * N + (size_t)sr * nl + c8) * 2) = v;
+            }
+        } else {
+            float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+            for (int sr = 0; sr < world; ++sr) {   // rank order
+                const float4 v = sr == rank ? reinterpret_cast<const float4*>(src)[u]
+                                            : ld_relaxed_sys_f4(reinterpret_cast<const float4*>(own + slot0 +
+                                                                                                 (uint64_t)sr * slot_bytes) + u);
+                a.x += v.x; a.y += v.y; a.z += v.z; a.w += v.w;
+            }
+            const __half2 h0 = __floats2half2_rn(a.x, a.y), h1 = __floats2half2_rn(a.z, a.w);
+            *reinterpret_cast<uint2*>(own + y_off + (size_t)u * 8) =
+                make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+        }
+    }
+    __syncthreads();
+    if (tid == 0) *epoch = e;
+}
+
+cudaError_t launch_tp_exchange(bool gather, bool push, const TpPtrs& p, int rank, int world, uint64_t src_off,
+                               uint64_t y_off, uint64_t recv_off, uint64_t slot_bytes, int M, int N,
+                               cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kTpCtas, 1, 1);
     cfg.blockDim = dim3(kTpThreads, 1, 1);
@@ -203,6 +291,11 @@ cudaError_t launch_tp_exchange(bool gather, const TpPtrs& p, int rank, int world
     attr.val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = &attr;
     cfg.numAttrs = 1;
+    if (push) {
+        if (gather)
+            return cudaLaunchKernelEx(&cfg, tp_push_kernel<true>, p, rank, world, src_off, y_off, recv_off, slot_bytes, M, N);
+        return cudaLaunchKernelEx(&cfg, tp_push_kernel<false>, p, rank, world, src_off, y_off, recv_off, slot_bytes, M, N);
+    }
     if (gather) return cudaLaunchKernelEx(&cfg, tp_exchange_kernel<true>, p, rank, world, src_off, y_off, M, N);
     return cudaLaunchKernelEx(&cfg, tp_exchange_kernel<false>, p, rank, world, src_off, y_off, M, N);
 }

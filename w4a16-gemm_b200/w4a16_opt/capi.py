@@ -27,6 +27,7 @@ STATUS_NAMES = {
 }
 TP_MAX_RANKS = 8
 TP_CTRL_BYTES = 8192
+TP_PUSH_MAX_BYTES = 1 << 20
 
 
 class Route(ctypes.Structure):
@@ -44,7 +45,7 @@ class IpcHandle(ctypes.Structure):
 
 class TpGroup(ctypes.Structure):
     _fields_ = [("rank", ctypes.c_int32), ("world", ctypes.c_int32), ("buf", ctypes.c_void_p * TP_MAX_RANKS),
-                ("buf_bytes", ctypes.c_uint64)]
+                ("buf_bytes", ctypes.c_uint64), ("recv_off", ctypes.c_uint64), ("recv_bytes", ctypes.c_uint64)]
 
 # name -> (restype, argtypes), one entry per declaration in include/w4a16.h
 EXPORTS = {

@@ -47,12 +47,15 @@ class PeerExchange:
 
     Layout of each buffer: the exchange's flags (``TP_CTRL_BYTES``), then a source region of
     ``src_bytes`` (this rank's GEMM output: fp32 partials or fp16 columns), then a result
-    region of ``y_bytes`` (fp16 y, written by every rank).  Layers sharing one exchange must
+    region of ``y_bytes`` (fp16 y), then a receive area of 2 * world slots of
+    ``min(src_bytes, push_bytes)`` (``push_bytes`` at most ``TP_PUSH_MAX_BYTES``; 0: no
+    receive area): exchanges whose per-rank contribution fits a slot (decode sizes) run in one
+    round through it, larger ones in two rounds, with the same results.  Layers sharing one exchange must
     be called in the same order on every rank, on one stream each; a result view stays valid
     until the next exchange.  ``close()`` unmaps and frees (collective).
     """
 
-    def __init__(self, src_bytes: int, y_bytes: int, group=None):
+    def __init__(self, src_bytes: int, y_bytes: int, group=None, push_bytes: Optional[int] = None):
         from . import capi
         import ctypes
         self._capi, self._ct = capi, ctypes
@@ -64,7 +67,11 @@ class PeerExchange:
             raise ValueError(f"at most {capi.TP_MAX_RANKS} ranks")
         self.src_off = capi.TP_CTRL_BYTES
         self.y_off = self.src_off + (int(src_bytes) + 255) // 256 * 256
-        self.nbytes = self.y_off + (int(y_bytes) + 255) // 256 * 256
+        self.recv_off = self.y_off + (int(y_bytes) + 255) // 256 * 256
+        push = capi.TP_PUSH_MAX_BYTES if push_bytes is None else min(int(push_bytes), capi.TP_PUSH_MAX_BYTES)
+        slot = (min(int(src_bytes), push) + 255) // 256 * 256
+        self.recv_bytes = 2 * self.world * slot if self.world > 1 and push > 0 else 0
+        self.nbytes = self.recv_off + self.recv_bytes
         own = ctypes.c_void_p()
         handle = capi.IpcHandle()
         capi.check(self.lib.w4a16_peer_alloc(self.nbytes, ctypes.byref(own), ctypes.byref(handle)), self.lib)
@@ -81,7 +88,8 @@ class PeerExchange:
             capi.check(self.lib.w4a16_peer_open(ctypes.byref(h), ctypes.byref(p)), self.lib)
             self.ptrs.append(p.value)
         self.tp_group = capi.TpGroup(self.rank, self.world,
-                                     (ctypes.c_void_p * capi.TP_MAX_RANKS)(*self.ptrs), self.nbytes)
+                                     (ctypes.c_void_p * capi.TP_MAX_RANKS)(*self.ptrs), self.nbytes,
+                                     self.recv_off, self.recv_bytes)
         dist.barrier(group=group)   # every rank has mapped every buffer before the first exchange
 
     def view(self, offset: int, shape, dtype: torch.dtype) -> torch.Tensor:
