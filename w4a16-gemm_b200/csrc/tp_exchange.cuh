@@ -10,8 +10,10 @@
 //                         call e's results is in your buffer"
 //   epoch[cta]            u32, this rank's own count of calls, per CTA (every call launches
 //                         the same kTpCtas CTAs, of whatever size, so all epochs agree)
-// and the caller's data regions follow.  Call e of an exchange (e = epoch + 1, the same on
-// every rank: all ranks issue the same exchanges in the same order):
+// and the caller's data regions follow (source, result and, optionally, a receive area of
+// 2 * world slots used by the one-round form, tp_push_kernel, below).  Call e of an exchange
+// (e = epoch + 1, the same on every rank: all ranks issue the same exchanges in the same
+// order, and every call of either form advances the same per-CTA epochs), two-round form:
 //   A. every CTA writes ready[rank] = e into every buffer (after a system-scope fence), then
 //      waits until its own buffer shows ready[src] >= e for every src;
 //   B. reduce: the rank owns columns [rank*N/world, (rank+1)*N/world); its CTAs load those
