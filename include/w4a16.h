@@ -265,6 +265,13 @@ w4a16_status w4a16_tp_allgather(const w4a16_tp_group* group, uint64_t src_off, u
  * ran out (0 = none).  Synchronises the device.  reset != 0 clears it. */
 w4a16_status w4a16_device_status(int32_t* code, int32_t reset);
 
+/* Diagnostic of the bounded-wait policy: launches two one-thread kernels that each wait for
+ * an mbarrier phase nothing completes, with the busy-polling and the sleeping wait the GEMM
+ * kernels use.  Each wait gives up after its limit (about 2 s), records its code in the
+ * device status word (4, then 1) and returns; codes[0..1] receive the status word read after
+ * each kernel, which is then cleared.  Synchronises the device; takes about 4 s. */
+w4a16_status w4a16_check_wait_limits(int32_t* codes);
+
 /* Short name of a status code. */
 const char* w4a16_status_string(w4a16_status status);
 

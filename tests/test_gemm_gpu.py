@@ -473,6 +473,26 @@ def test_fp32_scale_onehot_exact(G):
             assert not y[:m - 1].any()
 
 
+def test_bounded_waits_run_out_and_report():
+    """The mbarrier waits the GEMM kernels use give up after their limit (about 2 s), record
+    their code in the device status word and return, leaving the context usable: a one-thread
+    kernel waits for a phase that nothing completes, once with busy polls and once with
+    sleeping polls (the reader clears the word after each)."""
+    import time
+    from w4a16_opt import capi, device_status
+    lib = capi.load()
+    assert device_status(reset=True) == 0
+    codes = (ctypes.c_int32 * 2)()
+    t0 = time.monotonic()
+    capi.check(lib.w4a16_check_wait_limits(codes), lib)
+    waited = time.monotonic() - t0
+    assert list(codes) == [4, 1]
+    assert 2.0 < waited < 60.0, waited
+    assert device_status() == 0
+    x = torch.ones(4, device="cuda")
+    assert float((x * 2).sum()) == 8.0
+
+
 def test_device_status_clean():
     """No kernel in this session hit a bounded-wait timeout."""
     from w4a16_opt import device_status

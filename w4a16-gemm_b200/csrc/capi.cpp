@@ -429,6 +429,23 @@ w4a16_status w4a16_device_status(int32_t* code, int32_t reset) {
     return ok();
 }
 
+w4a16_status w4a16_check_wait_limits(int32_t* codes) {
+    if (!codes) return fail(W4A16_ERR_NULL_POINTER, "codes must be non-null");
+    w4a16::DeviceInfo d;
+    w4a16_status s = check_device(&d);
+    if (s != W4A16_OK) return s;
+    int c = 0;
+    cudaError_t err = w4a16::read_device_status(&c, true);   // start from a clean status word
+    const int expect[2] = {4, 1};                             // the pipeline and weight-ring codes
+    for (int i = 0; i < 2 && err == cudaSuccess; ++i) {
+        err = w4a16::run_wait_limit_check(i == 1, expect[i]);
+        if (err == cudaSuccess) err = w4a16::read_device_status(&c, true);
+        codes[i] = c;
+    }
+    if (err != cudaSuccess) return fail(W4A16_ERR_CUDA, std::string("CUDA error: ") + cudaGetErrorString(err));
+    return ok();
+}
+
 const char* w4a16_status_string(w4a16_status status) {
     switch (status) {
         case W4A16_OK: return "W4A16_OK";

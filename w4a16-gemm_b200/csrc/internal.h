@@ -43,6 +43,9 @@ cudaError_t ensure_max_dynamic_smem(const void* func);
 // Read (and optionally clear) the device status word that bounded waits set on
 // timeout.  Synchronises with the device.
 cudaError_t read_device_status(int* code, bool reset);
+// Launches one kernel whose bounded mbarrier wait runs out (about kWaitLimitNs) and waits
+// for it; the wait records `code` in the device status word.
+cudaError_t run_wait_limit_check(bool sleeping, int code);
 
 // Built-in scratch of w4a16_gemm_noalloc: a device array of kNoAllocScratchBytes
 // compiled into the library.  Returns its address on the current device (looked up

@@ -73,6 +73,25 @@ cudaError_t read_device_status(int* code, bool reset) {
     return cudaMemcpyToSymbol(w4a16_device_status, &zero, sizeof(int));
 }
 
+// One thread waits for phase 0 of an mbarrier that nothing arrives at, with the wait the
+// GEMM kernels use (busy polls, or polls that sleep between tries): after the wait limit it
+// records `code` in the device status word and returns.
+__global__ void wait_limit_kernel(int sleeping, int code) {
+    __shared__ __align__(8) uint64_t bar;
+    if (threadIdx.x == 0) {
+        mbar_init(smem_u32(&bar), 1);
+        fence_mbar_init();
+        if (sleeping) mbar_wait_sleep(smem_u32(&bar), 0, code);
+        else mbar_wait(smem_u32(&bar), 0, code);
+    }
+}
+
+cudaError_t run_wait_limit_check(bool sleeping, int code) {
+    wait_limit_kernel<<<1, 32>>>(sleeping ? 1 : 0, code);
+    const cudaError_t err = cudaGetLastError();
+    return err != cudaSuccess ? err : cudaDeviceSynchronize();
+}
+
 static PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
     static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
     static std::once_flag once;

@@ -68,6 +68,7 @@ EXPORTS = {
     "w4a16_tp_allreduce": (_i32, [ctypes.POINTER(TpGroup), _u64, _u64, _i64, _i64, _vp]),
     "w4a16_tp_allgather": (_i32, [ctypes.POINTER(TpGroup), _u64, _u64, _i64, _i64, _vp]),
     "w4a16_device_status": (_i32, [ctypes.POINTER(_i32), _i32]),
+    "w4a16_check_wait_limits": (_i32, [ctypes.POINTER(_i32)]),
     "w4a16_status_string": (ctypes.c_char_p, [_i32]),
     "w4a16_last_error": (ctypes.c_char_p, []),
 }
