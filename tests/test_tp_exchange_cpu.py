@@ -2,9 +2,11 @@
 
 * A thread-per-(rank, CTA) emulation of the exchange kernels' protocols -- the two-round
   pull (ready flags, per-CTA done flags) and the one-round push (contributions stored into
-  parity slots of every peer's receive area, one per-CTA done flag), per-CTA epochs, waits
-  that accept a flag at or past the expected epoch -- over shared arrays that stand in for
-  the ranks' buffers; calls of both protocols interleave as the C ABI chooses them by size.  Random delays move the
+  parity slots of every peer's receive area, one per-CTA done flag), the rank's call count
+  (epoch) that the last CTA of a call to finish advances, grids of two sizes (the kernel
+  launches more CTAs for large contributions), waits that accept a flag at or past the
+  expected epoch -- over shared arrays that stand in for the ranks' buffers; calls of both
+  protocols and both grid sizes interleave as the C ABI chooses them by size.  Random delays move the
   threads of different ranks and calls past one another; every call must still produce the
   rank-order sum (reduce) or the column gather, on every rank.  A rank that stops joining
   (a stalled peer, injected on the host) must make the others' bounded waits end in an
@@ -19,7 +21,9 @@ import time
 import numpy as np
 import pytest
 
-CTAS = 4   # the kernel launches a fixed kTpCtas CTAs; a smaller fixed count keeps the emulation fast
+# the kernel launches kTpCtasSmall (one-round calls, small two-round calls) or kTpCtasLarge
+# CTAs (two-round calls of large contributions); smaller counts keep the emulation fast
+CTAS_SMALL, CTAS_LARGE = 2, 4
 
 
 class PeerTimeout(Exception):
@@ -27,13 +31,14 @@ class PeerTimeout(Exception):
 
 
 class Exchange:
-    """Every rank's buffer: ready[src], done[src][cta], epoch[cta], the source and y regions."""
+    """Every rank's buffer: ready[src], done[src][cta], epoch and count, the source and y regions."""
 
     def __init__(self, world, M, N, gather, limit_s=2.0):
         self.world, self.M, self.N, self.gather, self.limit = world, M, N, gather, limit_s
         self.ready = np.zeros((world, world), np.int64)          # [buffer][src]
-        self.done = np.zeros((world, world, CTAS), np.int64)     # [buffer][src][cta]
-        self.epoch = np.zeros((world, CTAS), np.int64)           # [rank][cta]
+        self.done = np.zeros((world, world, CTAS_LARGE), np.int64)   # [buffer][src][cta]
+        self.epoch = np.zeros(world, np.int64)                   # [rank]: calls completed
+        self.count = np.zeros(world, np.int64)                   # [rank]: CTAs of the current call done
         self.y = np.full((world, M, N), np.nan)
         # receive area: [buffer][parity][src] one contribution each (stale values start as NaN)
         shape = (M, N // world) if gather else (M, N)
@@ -50,18 +55,31 @@ class Exchange:
                 raise PeerTimeout()
             time.sleep(0.0005 * random.random())
 
-    def push_cta(self, rank, cta, src_regions):
+    def start(self, rank):
+        """A CTA reads the rank's call count once, when it starts."""
+        with self.lock:
+            return self.epoch[rank] + 1
+
+    def count_out(self, rank, e, grid):
+        """tp_count_out: the last CTA of the call to finish advances the rank's epoch."""
+        with self.lock:
+            self.count[rank] += 1
+            if self.count[rank] == grid:
+                self.count[rank] = 0
+                self.epoch[rank] = e
+
+    def push_cta(self, rank, cta, src_regions, grid=CTAS_SMALL):
         """One CTA of tp_push_kernel on `rank`: send this CTA's units of the contribution to
         slot (e & 1, rank) of every peer, one flag per peer, wait for CTA cta of every peer,
         build y from the own source region and the received slots."""
         W, M, N = self.world, self.M, self.N
-        e = self.epoch[rank, cta] + 1
+        e = self.start(rank)
         par = e & 1
         own = src_regions[rank]
         flat = own.reshape(-1)
         units = flat.size // (8 if self.gather else 4)                 # 16-byte units
         per = 8 if self.gather else 4
-        lo, hi = units * cta // CTAS * per, units * (cta + 1) // CTAS * per
+        lo, hi = units * cta // grid * per, units * (cta + 1) // grid * per
         for t in range(W):                                             # A: stores into every peer
             if t != rank:
                 self.recv[t, par, rank].reshape(-1)[lo:hi] = flat[lo:hi]
@@ -70,9 +88,13 @@ class Exchange:
             for t in range(W):
                 if t != rank:
                     self.done[t, rank, cta] = max(self.done[t, rank, cta], e)
-        for src in range(W):
-            if src != rank:
-                self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
+        try:
+            for src in range(W):
+                if src != rank:
+                    self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
+        except PeerTimeout:
+            self.count_out(rank, e, grid)
+            raise
         # C: y from the same units
         if self.gather:
             nl = N // W
@@ -86,21 +108,25 @@ class Exchange:
             for src in range(W):                                       # rank order
                 acc = acc + (own if src == rank else self.recv[rank, par, src]).reshape(-1)[lo:hi]
             self.y[rank].reshape(-1)[lo:hi] = np.float16(acc)
-        self.epoch[rank, cta] = e
+        self.count_out(rank, e, grid)
 
-    def cta(self, rank, cta, src_regions):
+    def cta(self, rank, cta, src_regions, grid=CTAS_SMALL):
         """One CTA of the exchange kernel on `rank` (phases A, B, C); src_regions[r] is rank
         r's source region for this call."""
         W, M, N = self.world, self.M, self.N
-        e = self.epoch[rank, cta] + 1
+        e = self.start(rank)
         with self.lock:                                           # A: ready into every buffer
             for t in range(W):
                 self.ready[t, rank] = max(self.ready[t, rank], e)
-        for src in range(W):
-            self.wait_at_least(lambda src=src: self.ready[rank, src], e)
+        try:
+            for src in range(W):
+                self.wait_at_least(lambda src=src: self.ready[rank, src], e)
+        except PeerTimeout:
+            self.count_out(rank, e, grid)
+            raise
         nl = N // W                                               # B: this CTA's share of the rank's columns
         units = M * (nl // 8)
-        for u in range(units * cta // CTAS, units * (cta + 1) // CTAS):
+        for u in range(units * cta // grid, units * (cta + 1) // grid):
             m, c8 = u // (nl // 8), (u % (nl // 8)) * 8
             cols = slice(rank * nl + c8, rank * nl + c8 + 8)
             if self.gather:
@@ -115,16 +141,19 @@ class Exchange:
         with self.lock:                                           # C: done into every buffer
             for t in range(W):
                 self.done[t, rank, cta] = max(self.done[t, rank, cta], e)
-        for src in range(W):
-            self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
-        self.epoch[rank, cta] = e
+        try:
+            for src in range(W):
+                self.wait_at_least(lambda src=src: self.done[rank, src, cta], e)
+        finally:
+            self.count_out(rank, e, grid)
 
 
-def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=()):
+def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=(), large=()):
     """Every rank issues the calls in order, with no host synchronisation between ranks (a
     fast rank runs ahead); each call's CTAs run as threads.  After each call a rank reads its
     own y: no peer may write the next call's results into it before this rank announced
-    that call.  Returns results[rank][call], or raises the first error."""
+    that call.  Calls in `push` take the one-round form (always the small grid), calls in
+    `large` the large grid.  Returns results[rank][call], or raises the first error."""
     results = [[] for _ in range(ex.world)]
     errors = []
 
@@ -132,7 +161,8 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=()):
         for i, src in enumerate(inputs):
             if rank == stall_rank and i == stall_call:
                 return                                            # stops joining: never starts call i
-            threads = [threading.Thread(target=_cta, args=(rank, c, src, i in push)) for c in range(CTAS)]
+            grid = CTAS_LARGE if i in large and i not in push else CTAS_SMALL
+            threads = [threading.Thread(target=_cta, args=(rank, c, src, i in push, grid)) for c in range(grid)]
             for t in threads:
                 t.start()
             for t in threads:
@@ -141,9 +171,9 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=()):
                 return
             results[rank].append(ex.y[rank].copy())
 
-    def _cta(rank, c, src, one_round):
+    def _cta(rank, c, src, one_round, grid):
         try:
-            (ex.push_cta if one_round else ex.cta)(rank, c, src)
+            (ex.push_cta if one_round else ex.cta)(rank, c, src, grid)
         except Exception as exc:                                  # noqa: BLE001
             errors.append(exc)
 
@@ -158,14 +188,15 @@ def run_calls(ex, inputs, stall_rank=None, stall_call=None, push=()):
     return results
 
 
-@pytest.mark.parametrize("mix", ["pull", "push", "mixed"])
+@pytest.mark.parametrize("mix", ["pull", "push", "mixed", "grids"])
 @pytest.mark.parametrize("world", [2, 3, 4])
 @pytest.mark.parametrize("gather", [False, True])
 def test_exchange_protocol_results(world, gather, mix):
     rng = np.random.default_rng(world)
     M, N = 3, 16 * world
     calls = 10
-    push = {"pull": (), "push": tuple(range(calls)), "mixed": (1, 2, 4, 7, 8)}[mix]
+    push = {"pull": (), "push": tuple(range(calls)), "mixed": (1, 2, 4, 7, 8), "grids": ()}[mix]
+    large = {"pull": (), "push": (), "mixed": (0, 3, 9), "grids": (1, 2, 5, 6, 9)}[mix]
     inputs = []
     for _ in range(calls):
         if gather:
@@ -173,7 +204,7 @@ def test_exchange_protocol_results(world, gather, mix):
         else:
             inputs.append([rng.standard_normal((M, N)).astype(np.float32) for _ in range(world)])
     ex = Exchange(world, M, N, gather)
-    results = run_calls(ex, inputs, push=push)
+    results = run_calls(ex, inputs, push=push, large=large)
     assert all(len(r) == len(inputs) for r in results)
     for i, src in enumerate(inputs):
         if gather:
@@ -185,7 +216,7 @@ def test_exchange_protocol_results(world, gather, mix):
             want = acc.astype(np.float16)
         for r in range(world):
             assert np.array_equal(results[r][i].astype(np.float16), want), f"rank {r}, call {i}"
-    assert (ex.epoch == len(inputs)).all()
+    assert (ex.epoch == len(inputs)).all() and (ex.count == 0).all()
 
 
 @pytest.mark.parametrize("push", [(), (0, 1, 2)])

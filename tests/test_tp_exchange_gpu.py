@@ -1,8 +1,10 @@
 """The tensor-parallel exchange kernels on one GPU, through the C ABI.
 
 * A one-rank group: the reduction is a cast of the rank's fp32 partial to fp16 and the
-  gather a copy, over several calls (the per-CTA epochs advance), in the two-round form
-  (no receive area) and the one-round form (a receive area).
+  gather a copy, over several calls that alternate decode sizes with contributions of
+  8-16 MiB, which run on the larger grid (the rank's call count advances the same way
+  whatever the grid), in the two-round form (no receive area) and the one-round form (a
+  receive area, used by the small calls).
 * A bounded wait that runs out: a two-rank group whose second buffer is memory of this GPU
   that no rank ever flags.  The kernel must give up after its wait limit (about 2 s),
   record kDevTimeoutPeer (7) in the device status word and return, leaving the context
@@ -33,16 +35,18 @@ def _view(ptr, shape, dtype):
 def test_one_rank_exchange(one_round, cuda_device):
     from w4a16_opt import capi
     lib = capi.load()
-    M, N = 16, 4096
+    N, Ms = 4096, (16, 1024)
+    M = max(Ms)
     src_off, y_off = capi.TP_CTRL_BYTES, capi.TP_CTRL_BYTES + M * N * 4
     recv_off = y_off + M * N * 2
-    recv_bytes = 2 * M * N * 4 if one_round else 0
+    recv_bytes = 2 * capi.TP_PUSH_MAX_BYTES if one_round else 0
     nbytes = recv_off + recv_bytes
     buf = _alloc(lib, capi, nbytes)
     g = capi.TpGroup(0, 1, (ctypes.c_void_p * capi.TP_MAX_RANKS)(buf), nbytes, recv_off, recv_bytes)
     stream = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
     try:
-        for i in range(3):
+        for i in range(6):
+            M = Ms[i % 2]
             part = torch.randn(M, N, device="cuda") * (i + 1)
             _view(buf + src_off, (M, N), torch.float32).copy_(part)
             capi.check(lib.w4a16_tp_allreduce(ctypes.byref(g), src_off, y_off, M, N, stream), lib)

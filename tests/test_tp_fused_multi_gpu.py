@@ -1,12 +1,13 @@
-"""The tensor-parallel layers with the peer-memory exchange, on 2 GPUs (skipped with fewer).
+"""The tensor-parallel layers with the peer-memory exchange, on 2 GPUs (skipped with fewer;
+W4A16_TEST_WORLD=N runs it on N GPUs, N <= 8).
 
-Two child processes, one per GPU, NCCL for set-up (handles, barriers) and for the
+One child process per GPU, NCCL for set-up (handles, barriers) and for the
 reference path.  For the column-parallel (N split, gather) and row-parallel (K split, fp32
 reduction) layers at decode and prefill batch sizes:
 * the fused path (GEMM into the exchange buffer + the library's exchange kernel) matches
   the CPU oracle within the tests' tolerance, with the one-round exchange (receive area)
   and the two-round one (none), which give the same bits;
-* it gives bitwise identical y on both ranks (every rank holds the same rank-order sums);
+* it gives bitwise identical y on every rank (every rank holds the same rank-order sums);
 * it matches the NCCL path (all_gather_into_tensor / all_reduce) within tolerance -- the
   reduction order of NCCL's all-reduce is its own, so not bit for bit.
 """
@@ -20,7 +21,8 @@ import torch.multiprocessing as mp
 
 pytestmark = pytest.mark.gpu
 
-WORLD = 2
+# ranks (GPUs) of the test; 2 by default, up to W4A16_TP_MAX_RANKS = 8 with W4A16_TEST_WORLD
+WORLD = int(os.environ.get("W4A16_TEST_WORLD", "2"))
 CASES = [(1, 1024, 2048), (16, 2048, 4096), (200, 512, 1024)]   # M, N, K
 
 
@@ -69,7 +71,7 @@ def _rank_main(rank, port, out):
     out[rank] = res
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason=f"needs {WORLD} GPUs")
 def test_fused_exchange_two_gpus():
     from helpers import assert_close, make_workload, ref_gemm
     ctx = mp.get_context("spawn")
@@ -97,6 +99,7 @@ def test_fused_exchange_two_gpus():
             assert np.array_equal(y_col_f, y_col_2) and np.array_equal(y_row_f, y_row_2)   # both protocols
             assert np.array_equal(y_col_f, y_col_n)           # the gather moves the same fp16 values
             assert_close(y_row_f, y_row_n.astype(np.float32))
-        for k in range(2):
-            assert np.array_equal(res[0][(M, N, K)][k], res[1][(M, N, K)][k])
+        for rank in range(1, WORLD):
+            for k in range(2):
+                assert np.array_equal(res[0][(M, N, K)][k], res[rank][(M, N, K)][k])
 

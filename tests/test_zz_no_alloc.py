@@ -40,6 +40,10 @@ def test_noalloc_matches_workspace_entry(M, N, K, uses_scratch, cuda_device):
     # the decode scratch is 2 partial slots of 16 KB per CTA: 4.6 MiB on 148 SMs, inside the
     # 6 MiB array whatever the shape (the array's size covers GPUs of up to 192 SMs)
     assert (nbytes.value > 0) == uses_scratch and nbytes.value <= 6 << 20
+    # the scratch shapes really split column groups (decode kernel + combine kernel), so the
+    # built-in array is read back by a second launch on every call
+    from w4a16_opt import query_route
+    assert query_route(M, N, K, K // G)["launches"] == (2 if uses_scratch else 1)
     ws = torch.empty(max(256, nbytes.value), dtype=torch.uint8, device="cuda")
     for rep in range(2):   # the built-in scratch is reused by consecutive calls
         x, q, s, Wp = make_workload(M, N, K, G, seed=100 * rep + M + N)

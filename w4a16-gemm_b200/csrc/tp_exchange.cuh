@@ -8,12 +8,15 @@
 //                         in place and I am ready to receive call e's results"
 //   done[src][cta]        u32, written by CTA cta of rank src into every buffer: "my part of
 //                         call e's results is in your buffer"
-//   epoch[cta]            u32, this rank's own count of calls, per CTA (every call launches
-//                         the same kTpCtas CTAs, of whatever size, so all epochs agree)
+//   epoch, count          u32 each: this rank's own count of calls, advanced by the last
+//                         CTA of each call to finish (tp_count_out), and how many CTAs of
+//                         the current call have finished
 // and the caller's data regions follow (source, result and, optionally, a receive area of
-// 2 * world slots used by the one-round form, tp_push_kernel, below).  Call e of an exchange
-// (e = epoch + 1, the same on every rank: all ranks issue the same exchanges in the same
-// order, and every call of either form advances the same per-CTA epochs), two-round form:
+// 2 * world slots used by the one-round form, tp_push_kernel, below).  A call launches
+// kTpCtasSmall or kTpCtasLarge CTAs, chosen from its size alone, so every rank launches the
+// same grid for the same call.  Call e of an exchange (e = epoch + 1, the same on every
+// rank: all ranks issue the same exchanges in the same order, and every call of either form
+// advances the epoch once), two-round form:
 //   A. every CTA writes ready[rank] = e into every buffer (after a system-scope fence), then
 //      waits until its own buffer shows ready[src] >= e for every src;
 //   B. reduce: the rank owns columns [rank*N/world, (rank+1)*N/world); its CTAs load those
@@ -21,7 +24,7 @@
 //      into every rank's y.  gather: its CTAs store their own columns into every rank's y;
 //   C. every CTA writes done[rank][cta] = e into every buffer (release, after its stores),
 //      then waits until its own buffer shows done[src][cta] >= e for every src -- CTA cta of
-//      each rank wrote the same share of that rank's columns -- and stores epoch = e.
+//      each rank wrote the same share of that rank's columns -- and counts itself out.
 // Comparing with >= makes a flag that a faster rank already moved to e + 1 still count;
 // no flag is ever reset, so CUDA-graph replays keep working.  A rank cannot overwrite a
 // peer's y (or read its partial) for call e + 1 before that peer has finished call e: it
@@ -39,16 +42,20 @@
 namespace w4a16 {
 
 constexpr int kTpMaxRanks = W4A16_TP_MAX_RANKS;
-// Every exchange launches the same kTpCtas CTAs, whatever its size, so that each CTA's
-// epoch counts every call and the ranks' epochs stay equal.
-constexpr int kTpCtas = 32;
-constexpr int kTpMaxCtas = kTpCtas;
+// CTAs per call.  Decode-size exchanges are bound by the flag rounds, which more CTAs only
+// lengthen; prefill-size ones by how much peer traffic each SM issues (B200, 2 GPUs, gather
+// of 117 MB per rank: 315 us with 32 CTAs, 201 us with 128), so contributions of at least
+// kTpLargeBytes per rank take the larger grid.
+constexpr int kTpCtasSmall = 32;
+constexpr int kTpCtasLarge = 128;
+constexpr uint64_t kTpLargeBytes = 8ull << 20;
+constexpr int kTpMaxCtas = kTpCtasLarge;
 constexpr int kTpThreads = 512;
 constexpr int kTpUnroll = 4;   // 8-column units a thread moves per round: their peer loads are in flight together
 constexpr uint32_t kTpReadyOff = 0;
 constexpr uint32_t kTpDoneOff = 1024;
-constexpr uint32_t kTpEpochOff = kTpDoneOff + kTpMaxRanks * kTpMaxCtas * 4;
-static_assert(kTpEpochOff + kTpMaxCtas * 4 <= W4A16_TP_CTRL_BYTES, "exchange flags fit the control region");
+constexpr uint32_t kTpEpochOff = kTpDoneOff + kTpMaxRanks * kTpMaxCtas * 4;   // epoch, then the count-out word
+static_assert(kTpEpochOff + 8 <= W4A16_TP_CTRL_BYTES, "exchange flags fit the control region");
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
     asm volatile("st.release.sys.global.u32 [%0], %1;" :: "l"(p), "r"(v) : "memory");
@@ -82,6 +89,19 @@ __device__ __forceinline__ void fence_acq_rel_sys() {
     asm volatile("fence.acq_rel.sys;" ::: "memory");
 }
 
+// Every CTA of a call counts itself out when it is done, also after a wait that ran out; the
+// last one to do so advances the rank's call count (epoch[0]) and clears the count
+// (epoch[1]).  A CTA reads the epoch once, at its start, before it counts out, so none can
+// see the new value early; the next call reads it after griddepcontrol.wait, when this grid
+// has completed.  So every CTA of a call agrees on e whatever the grid sizes of the calls.
+// Thread 0 only.
+__device__ __forceinline__ void tp_count_out(uint32_t* epoch, uint32_t e) {
+    if (atomicAdd(epoch + 1, 1u) + 1u == gridDim.x) {
+        epoch[1] = 0u;
+        epoch[0] = e;
+    }
+}
+
 // Bounded wait until *p >= e (as a difference, so the epoch may wrap).
 __device__ __forceinline__ bool wait_at_least(const uint32_t* p, uint32_t e) {
     if ((int32_t)(ld_acquire_sys(p) - e) >= 0) return true;
@@ -105,14 +125,14 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
     __shared__ int s_ok;
     const int cta = blockIdx.x, tid = threadIdx.x;
     char* const own = P.buf[rank];
-    uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff) + cta;
+    uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff);
     // Launched with programmatic dependent launch: the next kernel may start early (it waits
     // for this one), and this one waits here until the GEMM that wrote the source region has
     // completed and its writes are visible.
     pdl_launch_dependents();
     pdl_wait();
     if (tid == 0) {
-        s_e = *epoch + 1u;
+        s_e = *reinterpret_cast<volatile uint32_t*>(epoch) + 1u;
         s_ok = 1;
     }
     __syncthreads();
@@ -126,7 +146,10 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
     }
     if (tid < world && !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpReadyOff) + tid, e)) s_ok = 0;
     __syncthreads();
-    if (!s_ok) return;
+    if (!s_ok) {
+        if (tid == 0) tp_count_out(epoch, e);
+        return;
+    }
 
     // B. this CTA's share of this rank's columns, 8 at a time (16-byte peer accesses); a thread
     // moves kTpUnroll units per round, issuing their loads together
@@ -198,7 +221,7 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
     if (tid < world && !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpDoneOff) + tid * kTpMaxCtas + cta, e))
         s_ok = 0;
     __syncthreads();
-    if (tid == 0 && s_ok) *epoch = e;
+    if (tid == 0) tp_count_out(epoch, e);
 }
 
 // One-round form for small contributions: call e (parity e & 1) of rank r stores its
@@ -209,8 +232,9 @@ __global__ void __launch_bounds__(kTpThreads) tp_exchange_kernel(const __grid_co
 // places each rank's columns, the reduction adds the ranks' partials in rank order.  Each
 // CTA sends and then reads the same range of 16-byte units of a contribution, so CTA cta's
 // flags cover exactly the units it reads.  A slot of parity p is written again two calls
-// later, after the writer has seen this rank's CTA cta finish the call in between, which
-// this rank's CTA cta starts only after it read the slot.  One fence per CTA and call (the
+// later, after the writer has seen this rank's CTA cta finish the call in between (a
+// one-round call has the kTpCtasSmall CTAs that every call has), which this rank starts only
+// after the call that read the slot has completed.  One fence per CTA and call (the
 // two-round form needs two; each costs microseconds at system scope).
 template <bool GATHER>
 __global__ void __launch_bounds__(kTpThreads) tp_push_kernel(const __grid_constant__ TpPtrs P, int rank, int world,
@@ -220,11 +244,11 @@ __global__ void __launch_bounds__(kTpThreads) tp_push_kernel(const __grid_consta
     __shared__ int s_ok;
     const int cta = blockIdx.x, tid = threadIdx.x;
     char* const own = P.buf[rank];
-    uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff) + cta;
+    uint32_t* const epoch = reinterpret_cast<uint32_t*>(own + kTpEpochOff);
     pdl_launch_dependents();
     pdl_wait();   // the GEMM that wrote the source region has completed
     if (tid == 0) {
-        s_e = *epoch + 1u;
+        s_e = *reinterpret_cast<volatile uint32_t*>(epoch) + 1u;
         s_ok = 1;
     }
     __syncthreads();
@@ -252,7 +276,10 @@ __global__ void __launch_bounds__(kTpThreads) tp_push_kernel(const __grid_consta
         !wait_at_least(reinterpret_cast<const uint32_t*>(own + kTpDoneOff) + tid * kTpMaxCtas + cta, e))
         s_ok = 0;
     __syncthreads();
-    if (!s_ok) return;
+    if (!s_ok) {
+        if (tid == 0) tp_count_out(epoch, e);
+        return;
+    }
 
     // C. this rank's y from the same units: own source region and the received slots
     for (long long u = u0 + tid; u < u1; u += kTpThreads) {
@@ -278,14 +305,15 @@ __global__ void __launch_bounds__(kTpThreads) tp_push_kernel(const __grid_consta
         }
     }
     __syncthreads();
-    if (tid == 0) *epoch = e;
+    if (tid == 0) tp_count_out(epoch, e);
 }
 
 cudaError_t launch_tp_exchange(bool gather, bool push, const TpPtrs& p, int rank, int world, uint64_t src_off,
                                uint64_t y_off, uint64_t recv_off, uint64_t slot_bytes, int M, int N,
                                cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kTpCtas, 1, 1);
+    const uint64_t contribution = gather ? (uint64_t)M * (uint64_t)(N / world) * 2u : (uint64_t)M * (uint64_t)N * 4u;
+    cfg.gridDim = dim3(!push && contribution >= kTpLargeBytes ? kTpCtasLarge : kTpCtasSmall, 1, 1);
     cfg.blockDim = dim3(kTpThreads, 1, 1);
     cfg.stream = stream;
     cudaLaunchAttribute attr;
